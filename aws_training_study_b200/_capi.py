@@ -1,0 +1,123 @@
+"""ctypes binding of ``libpcp_attn.so`` (the C ABI in ``include/pcp_attn.h``).
+
+There is no fallback: if the library is missing this module raises
+``ImportError`` with the build command, and every product entry point goes
+through it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libpcp_attn.so")
+
+PCP_KV_E4M3 = 0
+PCP_KV_BF16 = 1
+
+STATUS_NAMES = {
+    0: "PCP_OK",
+    1: "PCP_ERR_INVALID_ARGUMENT",
+    2: "PCP_ERR_UNSUPPORTED",
+    3: "PCP_ERR_CUDA",
+    4: "PCP_ERR_NCCL",
+    5: "PCP_ERR_DEVICE_TIMEOUT",
+    6: "PCP_ERR_OUT_OF_MEMORY",
+    7: "PCP_ERR_PEER",
+}
+
+# Every function declared in include/pcp_attn.h: name -> (restype, argtypes).
+_c = ctypes
+_P = _c.c_void_p
+_I32 = _c.c_int32
+_PI32 = _c.POINTER(_c.c_int32)
+
+
+class PcpDims(ctypes.Structure):
+    _fields_ = [
+        ("pcp_size", _I32),
+        ("local_q_len", _I32),
+        ("max_local_blocks", _I32),
+        ("block_size", _I32),
+        ("num_q_heads", _I32),
+        ("num_kv_heads", _I32),
+        ("head_dim", _I32),
+        ("kv_dtype", _I32),
+    ]
+
+
+class PcpStats(ctypes.Structure):
+    _fields_ = [
+        ("attn_ms", _c.c_double),
+        ("unpack_ms", _c.c_double),
+        ("combine_ms", _c.c_double),
+        ("comm_ms", _c.c_double),
+        ("kernel_launches", _I32),
+        ("attn_launches", _I32),
+        ("splits", _I32),
+        ("reserved", _I32),
+        ("ring_bytes", _c.c_int64),
+        ("keys", _c.c_int64),
+    ]
+
+
+_PDIMS = _c.POINTER(PcpDims)
+
+SIGNATURES = {
+    "pcp_last_error": (_c.c_char_p, []),
+    "pcp_abi_version": (_c.c_int, []),
+    "pcp_source_valid_len": (_c.c_int64, [_c.c_int64, _I32, _I32, _I32]),
+    "pcp_ring_schedule": (_c.c_int, [_I32, _I32, _I32, _PI32, _PI32, _PI32, _PI32]),
+    "pcp_nccl_unique_id_bytes": (_c.c_int, []),
+    "pcp_get_nccl_unique_id": (_c.c_int, [_P]),
+    "pcp_history_attention_workspace_size": (_c.c_int, [_PDIMS, _c.c_int64, _c.POINTER(_c.c_size_t)]),
+    "pcp_history_attention": (_c.c_int, [_PDIMS, _P, _P, _I32, _PI32, _P, _P, _c.c_size_t, _P]),
+    "pcp_history_attention_status": (_c.c_int, [_P, _P]),
+    "pcp_selftest_bounded_wait": (_c.c_int, [_I32, _PI32]),
+    "pcp_create": (_c.c_int, [_PDIMS, _I32, _I32, _P, _c.POINTER(_P)]),
+    "pcp_forward": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_device_status": (_c.c_int, [_P, _I32]),
+    "pcp_set_profiling": (_c.c_int, [_P, _I32]),
+    "pcp_get_stats": (_c.c_int, [_P, _c.POINTER(PcpStats)]),
+    "pcp_destroy": (_c.c_int, [_P]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the extension (once).  Raises ImportError when it was not built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise ImportError(
+                    f"{LIB_PATH} is missing: build it with `python -m aws_training_study_b200.build` "
+                    "(the CUDA path has no fallback)"
+                )
+            handle = ctypes.CDLL(str(LIB_PATH))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = handle
+    return _lib
+
+
+class PcpError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise PcpError(status, lib().pcp_last_error().decode(errors="replace"))
+
+
+def int32_array(values) -> ctypes.Array:
+    vals = [int(v) for v in values]
+    return (ctypes.c_int32 * len(vals))(*vals)

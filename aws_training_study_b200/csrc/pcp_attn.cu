@@ -1,0 +1,767 @@
+// Host side of the C ABI declared in include/pcp_attn.h: launch planning,
+// TMA tensor maps, the stateless single-GPU entry, and the per-rank ring
+// handle (NCCL send/recv ring on a high-priority stream overlapped with the
+// attention of the local shard).
+#include "pcp_attn.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "attn_fwd.cuh"
+#include "kv_stage.cuh"
+
+namespace {
+
+thread_local char g_err[1024] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define CUDA_TRY(x)                                                                                     \
+  do {                                                                                                  \
+    cudaError_t e_ = (x);                                                                               \
+    if (e_ != cudaSuccess)                                                                              \
+      return fail(e_ == cudaErrorMemoryAllocation ? PCP_ERR_OUT_OF_MEMORY : PCP_ERR_CUDA, "%s: %s (%s:%d)", \
+                  #x, cudaGetErrorString(e_), __FILE__, __LINE__);                                     \
+  } while (0)
+
+#define PCP_TRY(x)          \
+  do {                      \
+    int s_ = (x);           \
+    if (s_ != PCP_OK) return s_; \
+  } while (0)
+
+constexpr int kMaxTotalSplits = 32;
+constexpr size_t kPartialBudget = size_t(1) << 30;  // bytes of split partials a handle may hold
+
+// ------------------------------------------------------------ tensor maps --
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor [heads][rows][cols] (cols contiguous, heads `head_stride` elements
+// apart), boxes of 64 cols x 128 rows x 1 head with 128-byte swizzle.
+int make_tmap(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t heads,
+              uint64_t head_stride) {
+  auto fn = encode_fn();
+  if (!fn) return fail(PCP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(PCP_ERR_INVALID_ARGUMENT, "TMA base not 16-byte aligned");
+  cuuint64_t dims[3] = {cols, rows, heads};
+  cuuint64_t strides[2] = {cols * 2, head_stride * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PCP_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return PCP_OK;
+}
+
+// --------------------------------------------------------------- planning --
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
+
+struct SplitPlan {
+  int splits = 1;
+  int tiles_per_split = 1;
+};
+
+// Choose how many key splits a launch uses so that (work units) fill whole
+// waves of the SMs.  Cost model: waves * (tiles per unit + 2 tiles of fixed
+// prologue/epilogue cost), with a small bias against splitting.
+SplitPlan plan_splits(int64_t m_units, int64_t n_kt, int sms, int max_splits) {
+  SplitPlan best;
+  best.splits = 1;
+  best.tiles_per_split = static_cast<int>(n_kt);
+  double best_cost = 1e300;
+  const int smax = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_splits, n_kt)));
+  for (int s = 1; s <= smax; ++s) {
+    const int64_t tps = ceil_div(n_kt, s);
+    const int64_t s_eff = ceil_div(n_kt, tps);
+    const int64_t waves = ceil_div(m_units * s_eff, sms);
+    const double cost = static_cast<double>(waves) * (static_cast<double>(tps) + 2.0) + (s_eff > 1 ? 0.5 : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best.splits = static_cast<int>(s_eff);
+      best.tiles_per_split = static_cast<int>(tps);
+    }
+  }
+  return best;
+}
+
+int check_dims(const pcp_dims_t* d) {
+  if (!d) return fail(PCP_ERR_INVALID_ARGUMENT, "dims is NULL");
+  if (d->pcp_size <= 0 || d->local_q_len <= 0 || d->max_local_blocks <= 0 || d->block_size <= 0 ||
+      d->num_q_heads <= 0 || d->num_kv_heads <= 0 || d->head_dim <= 0)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "all dims must be positive");
+  if (d->num_q_heads % d->num_kv_heads)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "num_q_heads must be divisible by num_kv_heads");
+  if (d->head_dim != 128 && d->head_dim != 256)
+    return fail(PCP_ERR_UNSUPPORTED, "head_dim %d unsupported by the CUDA kernel (128 or 256)", d->head_dim);
+  if (d->kv_dtype != PCP_KV_E4M3 && d->kv_dtype != PCP_KV_BF16)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "kv_dtype %d unknown", d->kv_dtype);
+  if (d->pcp_size > pcp::kMaxSources) return fail(PCP_ERR_UNSUPPORTED, "pcp_size above %d", pcp::kMaxSources);
+  const int64_t rows = static_cast<int64_t>(d->num_q_heads / d->num_kv_heads) * d->local_q_len;
+  if (rows > (int64_t(1) << 30)) return fail(PCP_ERR_UNSUPPORTED, "too many query rows per KV head");
+  return PCP_OK;
+}
+
+int64_t payload_bytes(const pcp_dims_t& d) {
+  return 2LL * d.num_kv_heads * d.block_size * d.head_dim * (d.kv_dtype == PCP_KV_BF16 ? 2 : 1);
+}
+int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads / d.num_kv_heads) * d.local_q_len; }
+int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
+int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kTileM); }
+
+int num_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+int max_splits_for(const pcp_dims_t& d) {
+  const size_t per_split = static_cast<size_t>(total_rows(d)) * d.head_dim * 4 + static_cast<size_t>(total_rows(d)) * 4;
+  const size_t cap = std::max<size_t>(2, kPartialBudget / std::max<size_t>(per_split, 1));
+  return static_cast<int>(std::min<size_t>(kMaxTotalSplits, cap));
+}
+
+// Workspace: [error word][K bf16][V bf16][partial O fp32][partial lse fp32].
+struct Workspace {
+  size_t k_off = 0, v_off = 0, po_off = 0, pl_off = 0, total = 0;
+  int64_t key_stride = 0;
+  int max_splits = 0;
+};
+
+Workspace ws_layout(const pcp_dims_t& d, int64_t key_cap, int split_cap) {
+  Workspace w;
+  w.key_stride = align_up(static_cast<size_t>(std::max<int64_t>(key_cap, 1)), pcp::kTileN);
+  const size_t kv = static_cast<size_t>(d.num_kv_heads) * w.key_stride * d.head_dim * 2;
+  w.k_off = 1024;
+  w.v_off = align_up(w.k_off + kv, 1024);
+  w.po_off = align_up(w.v_off + kv, 1024);
+  w.max_splits = split_cap;
+  const size_t po = split_cap > 1 ? static_cast<size_t>(split_cap) * total_rows(d) * d.head_dim * 4 : 0;
+  w.pl_off = align_up(w.po_off + po, 1024);
+  const size_t pl = split_cap > 1 ? static_cast<size_t>(split_cap) * total_rows(d) * 4 : 0;
+  w.total = align_up(w.pl_off + pl, 1024);
+  return w;
+}
+
+template <int D>
+int set_smem_attr() {
+  static int done = 0;
+  static int status = PCP_OK;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done & (1 << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(pcp::attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pcp::AttnSmem<D>::kAlloc);
+    if (e != cudaSuccess) return fail(PCP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done |= (1 << dev);
+  }
+  return status;
+}
+
+struct LaunchCounter {
+  int kernels = 0;
+  int attn = 0;
+};
+
+int launch_unpack(const pcp_dims_t& d, const std::vector<pcp::UnpackSource>& srcs, const Workspace& w, uint8_t* ws,
+                  cudaStream_t st, LaunchCounter* lc) {
+  if (srcs.empty()) return PCP_OK;
+  if (srcs.size() > static_cast<size_t>(pcp::kMaxSources)) return fail(PCP_ERR_UNSUPPORTED, "too many sources");
+  pcp::UnpackParams p{};
+  int max_valid = 0;
+  for (size_t i = 0; i < srcs.size(); ++i) {
+    p.src[i] = srcs[i];
+    max_valid = std::max(max_valid, srcs[i].valid);
+    if (reinterpret_cast<uintptr_t>(srcs[i].base) % 16)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "packed_kv must be 16-byte aligned");
+  }
+  p.num_sources = static_cast<int>(srcs.size());
+  p.num_kv_heads = d.num_kv_heads;
+  p.block_size = d.block_size;
+  p.head_dim = d.head_dim;
+  p.kv_is_bf16 = d.kv_dtype == PCP_KV_BF16;
+  p.key_stride = static_cast<int>(w.key_stride);
+  p.k_out = reinterpret_cast<__nv_bfloat16*>(ws + w.k_off);
+  p.v_out = reinterpret_cast<__nv_bfloat16*>(ws + w.v_off);
+  const int64_t live_blocks = ceil_div(max_valid, d.block_size);
+  const int64_t items = live_blocks * 2 * d.num_kv_heads * d.block_size * (d.head_dim / 16);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 4 * 148));
+  dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(srcs.size()));
+  pcp::kv_unpack_kernel<<<grid, 256, 0, st>>>(p);
+  CUDA_TRY(cudaGetLastError());
+  if (lc) lc->kernels++;
+  return PCP_OK;
+}
+
+// Attention over `num_keys` dense keys starting at key `key_off` of the
+// workspace K/V.  Writes bf16 `out` directly (final) or split partials.
+int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uint8_t* ws, int64_t key_off,
+                     int64_t num_keys, const SplitPlan& plan, int split_base, bool final_out, void* out,
+                     cudaStream_t st, LaunchCounter* lc) {
+  const int64_t R = rows_per_head(d);
+  const int64_t mt = ceil_div(R, pcp::kTileM);
+  CUtensorMap tq, tk, tv, to;
+  const auto* kb = reinterpret_cast<const __nv_bfloat16*>(ws + w.k_off) + key_off * d.head_dim;
+  const auto* vb = reinterpret_cast<const __nv_bfloat16*>(ws + w.v_off) + key_off * d.head_dim;
+  PCP_TRY(make_tmap(&tq, q, d.head_dim, R, d.num_kv_heads, R * d.head_dim));
+  PCP_TRY(make_tmap(&tk, kb, d.head_dim, num_keys, d.num_kv_heads, w.key_stride * d.head_dim));
+  PCP_TRY(make_tmap(&tv, vb, d.head_dim, num_keys, d.num_kv_heads, w.key_stride * d.head_dim));
+  PCP_TRY(make_tmap(&to, final_out ? out : q, d.head_dim, R, d.num_kv_heads, R * d.head_dim));
+  pcp::AttnParams p{};
+  p.rows_per_head = static_cast<int>(R);
+  p.m_tiles_per_head = static_cast<int>(mt);
+  p.num_kv_heads = d.num_kv_heads;
+  p.num_keys = static_cast<int>(num_keys);
+  p.tiles_per_split = plan.tiles_per_split;
+  p.split_base = split_base;
+  p.total_rows = static_cast<int>(total_rows(d));
+  p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d.head_dim)) * 1.4426950408889634);
+  p.write_final = final_out ? 1 : 0;
+  p.part_o = reinterpret_cast<float*>(ws + w.po_off);
+  p.part_lse = reinterpret_cast<float*>(ws + w.pl_off);
+  p.err = reinterpret_cast<int*>(ws);
+  dim3 grid(static_cast<unsigned>(d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
+  if (d.head_dim == 256) {
+    PCP_TRY(set_smem_attr<256>());
+    pcp::attn_fwd_kernel<256><<<grid, 192, pcp::AttnSmem<256>::kAlloc, st>>>(tq, tk, tv, to, p);
+  } else {
+    PCP_TRY(set_smem_attr<128>());
+    pcp::attn_fwd_kernel<128><<<grid, 192, pcp::AttnSmem<128>::kAlloc, st>>>(tq, tk, tv, to, p);
+  }
+  CUDA_TRY(cudaGetLastError());
+  if (lc) {
+    lc->kernels++;
+    lc->attn++;
+  }
+  return PCP_OK;
+}
+
+int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int splits, void* out, cudaStream_t st,
+                   LaunchCounter* lc) {
+  pcp::CombineParams p{};
+  p.part_o = reinterpret_cast<const float*>(ws + w.po_off);
+  p.part_lse = reinterpret_cast<const float*>(ws + w.pl_off);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.num_splits = splits;
+  p.rows = static_cast<int>(total_rows(d));
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(p.rows, 8), 16 * 148));
+  if (d.head_dim == 256)
+    pcp::combine_kernel<256><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  else
+    pcp::combine_kernel<128><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  CUDA_TRY(cudaGetLastError());
+  if (lc) lc->kernels++;
+  return PCP_OK;
+}
+
+// One attention "part" = a set of sources unpacked into a key range, then
+// attended in one launch.
+struct Part {
+  std::vector<pcp::UnpackSource> srcs;
+  int64_t key_off = 0;
+  int64_t keys = 0;
+  SplitPlan plan;
+};
+
+int plan_part(const pcp_dims_t& d, Part* part, int sms, int max_splits) {
+  const int64_t n_kt = ceil_div(part->keys, pcp::kTileN);
+  if (n_kt == 0) return PCP_OK;
+  part->plan = plan_splits(m_units(d), n_kt, sms, max_splits);
+  return PCP_OK;
+}
+
+// ---------------------------------------------------------- bounded-wait probe --
+__global__ void bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    pcp::mbar_init(pcp::smem_u32(&bar), 1);
+    pcp::fence_mbar_init();
+  }
+  __syncthreads();
+  // Nothing ever arrives on `bar`: the wait must give up by itself.
+  if (threadIdx.x == 0) {
+    const uint32_t b = pcp::smem_u32(&bar);
+    const uint64_t t0 = pcp::globaltimer_ns();
+    bool done = false;
+    while (!done) {
+      if (pcp::mbar_try_wait(b, 0)) break;
+      if (pcp::globaltimer_ns() - t0 > limit_ns) {
+        atomicCAS(err, 0, 199);
+        done = true;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
+// ============================================================ C ABI ======
+struct pcp_handle {
+  pcp_dims_t d{};
+  int rank = 0;
+  int device = 0;
+  int sms = 148;
+  ncclComm_t comm = nullptr;
+  bool comm_failed = false;
+  cudaStream_t comm_stream = nullptr;
+  cudaStream_t last_stream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_comm = nullptr;
+  uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]
+  uint8_t* ws = nullptr;
+  Workspace w;
+  // staging for pcp_forward_host
+  void* dq = nullptr;
+  void* dkv = nullptr;
+  void* dout = nullptr;
+  bool profiling = false;
+  // profiling events: comm(2) unpackA(2) attnA(2) unpackB(2) attnB(2) combine(2)
+  cudaEvent_t pev[12] = {};
+  bool pev_used[6] = {};
+  pcp_stats_t stats{};
+};
+
+namespace {
+
+int wait_nccl(ncclComm_t comm, ncclResult_t r, int timeout_ms) {
+  if (r == ncclSuccess) return PCP_OK;
+  if (r != ncclInProgress) return fail(PCP_ERR_NCCL, "NCCL: %s", ncclGetErrorString(r));
+  const auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t st = ncclInProgress;
+  while (true) {
+    ncclCommGetAsyncError(comm, &st);
+    if (st != ncclInProgress) break;
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      return fail(PCP_ERR_PEER, "NCCL operation still in progress after %d ms (peer missing?)", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+  if (st != ncclSuccess) return fail(PCP_ERR_NCCL, "NCCL async error: %s", ncclGetErrorString(st));
+  return PCP_OK;
+}
+
+void prof_record(pcp_handle* h, int slot, bool end, cudaStream_t st) {
+  if (!h->profiling) return;
+  cudaEventRecord(h->pev[2 * slot + (end ? 1 : 0)], st);
+  h->pev_used[slot] = true;
+}
+
+int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
+                 cudaStream_t st) {
+  const pcp_dims_t& d = h->d;
+  const int P = d.pcp_size;
+  const int r = h->rank;
+  if (!q || !packed_kv || !valid_len || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  int64_t total = 0;
+  for (int s = 0; s < P; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    total += valid_len[s];
+  }
+  if (total == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  CUDA_TRY(cudaSetDevice(h->device));
+  h->last_stream = st;
+  for (bool& u : h->pev_used) u = false;
+  LaunchCounter lc;
+  const int64_t pay = payload_bytes(d);
+  const int max_splits = h->w.max_splits;
+
+  Part local, remote;
+  local.key_off = 0;
+  local.keys = valid_len[r];
+  if (valid_len[r] > 0) local.srcs.push_back({static_cast<const uint8_t*>(packed_kv), valid_len[r], 0});
+  remote.key_off = local.keys;
+  int64_t sent = 0;
+  if (P > 1) {
+    CUDA_TRY(cudaEventRecord(h->ev_in, st));
+    CUDA_TRY(cudaStreamWaitEvent(h->comm_stream, h->ev_in, 0));
+    prof_record(h, 0, false, h->comm_stream);
+    for (int hop = 1; hop < P; ++hop) {
+      const int ssrc = ((r - hop + 1) % P + P) % P;
+      const int rsrc = ((r - hop) % P + P) % P;
+      const void* sbuf = hop == 1 ? packed_kv : h->ring + static_cast<size_t>(ssrc) * d.max_local_blocks * pay;
+      void* rbuf = h->ring + static_cast<size_t>(rsrc) * d.max_local_blocks * pay;
+      const size_t sbytes = static_cast<size_t>(ceil_div(valid_len[ssrc], d.block_size)) * pay;
+      const size_t rbytes = static_cast<size_t>(ceil_div(valid_len[rsrc], d.block_size)) * pay;
+      ncclResult_t nr = ncclGroupStart();
+      if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
+      if (sbytes) ncclSend(sbuf, sbytes, ncclUint8, (r + 1) % P, h->comm, h->comm_stream);
+      if (rbytes) ncclRecv(rbuf, rbytes, ncclUint8, (r - 1 + P) % P, h->comm, h->comm_stream);
+      PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
+      sent += static_cast<int64_t>(sbytes);
+      if (valid_len[rsrc] > 0)
+        remote.srcs.push_back({static_cast<const uint8_t*>(rbuf), valid_len[rsrc],
+                               static_cast<int>(remote.key_off + remote.keys)});
+      remote.keys += valid_len[rsrc];
+    }
+    prof_record(h, 0, true, h->comm_stream);
+    CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
+  }
+  plan_part(d, &local, h->sms, max_splits);
+  plan_part(d, &remote, h->sms, max_splits);
+  int splits_local = local.keys ? local.plan.splits : 0;
+  int splits_remote = remote.keys ? remote.plan.splits : 0;
+  if (splits_local + splits_remote > max_splits) {
+    // Keep the total within the partial buffers: shrink the larger part.
+    Part& big = splits_local >= splits_remote ? local : remote;
+    const int other = (&big == &local) ? splits_remote : splits_local;
+    big.plan = plan_splits(m_units(d), ceil_div(big.keys, pcp::kTileN), h->sms, std::max(1, max_splits - other));
+    splits_local = local.keys ? local.plan.splits : 0;
+    splits_remote = remote.keys ? remote.plan.splits : 0;
+  }
+  const int total_splits = splits_local + splits_remote;
+  const bool direct = total_splits == 1;
+  CUDA_TRY(cudaMemsetAsync(h->ws, 0, 4, st));
+
+  if (local.keys) {
+    prof_record(h, 1, false, st);
+    PCP_TRY(launch_unpack(d, local.srcs, h->w, h->ws, st, &lc));
+    prof_record(h, 1, true, st);
+    prof_record(h, 2, false, st);
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, local.key_off, local.keys, local.plan, 0, direct, out, st, &lc));
+    prof_record(h, 2, true, st);
+  }
+  if (P > 1) CUDA_TRY(cudaStreamWaitEvent(st, h->ev_comm, 0));
+  if (remote.keys) {
+    prof_record(h, 3, false, st);
+    PCP_TRY(launch_unpack(d, remote.srcs, h->w, h->ws, st, &lc));
+    prof_record(h, 3, true, st);
+    prof_record(h, 4, false, st);
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, remote.key_off, remote.keys, remote.plan, splits_local, direct, out,
+                             st, &lc));
+    prof_record(h, 4, true, st);
+  }
+  if (!direct) {
+    prof_record(h, 5, false, st);
+    PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc));
+    prof_record(h, 5, true, st);
+  }
+  h->stats = pcp_stats_t{};
+  h->stats.kernel_launches = lc.kernels;
+  h->stats.attn_launches = lc.attn;
+  h->stats.splits = total_splits;
+  h->stats.ring_bytes = sent;
+  h->stats.keys = total;
+  return PCP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pcp_last_error(void) { return g_err; }
+
+int pcp_abi_version(void) { return PCP_ATTN_ABI_VERSION; }
+
+int64_t pcp_source_valid_len(int64_t total_len, int32_t pcp_size, int32_t interleave_size, int32_t rank) {
+  if (total_len < 0 || pcp_size <= 0 || interleave_size <= 0 || rank < 0 || rank >= pcp_size) return -1;
+  const int64_t stride = static_cast<int64_t>(pcp_size) * interleave_size;
+  const int64_t full = total_len / stride, tail = total_len % stride;
+  const int64_t extra = std::min<int64_t>(std::max<int64_t>(tail - static_cast<int64_t>(rank) * interleave_size, 0),
+                                          interleave_size);
+  return full * interleave_size + extra;
+}
+
+int pcp_ring_schedule(int32_t rank, int32_t pcp_size, int32_t hop, int32_t* send_source, int32_t* recv_source,
+                      int32_t* send_to, int32_t* recv_from) {
+  if (pcp_size <= 0 || rank < 0 || rank >= pcp_size || hop < 1 || hop >= pcp_size)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "hop %d outside [1, %d) or rank %d outside [0, %d)", hop, pcp_size, rank,
+                pcp_size);
+  if (send_source) *send_source = ((rank - hop + 1) % pcp_size + pcp_size) % pcp_size;
+  if (recv_source) *recv_source = ((rank - hop) % pcp_size + pcp_size) % pcp_size;
+  if (send_to) *send_to = (rank + 1) % pcp_size;
+  if (recv_from) *recv_from = (rank - 1 + pcp_size) % pcp_size;
+  return PCP_OK;
+}
+
+int pcp_nccl_unique_id_bytes(void) { return static_cast<int>(sizeof(ncclUniqueId)); }
+
+int pcp_get_nccl_unique_id(void* out) {
+  if (!out) return fail(PCP_ERR_INVALID_ARGUMENT, "out is NULL");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  std::memcpy(out, &id, sizeof(id));
+  return PCP_OK;
+}
+
+int pcp_history_attention_workspace_size(const pcp_dims_t* dims, int64_t total_valid, size_t* bytes) {
+  PCP_TRY(check_dims(dims));
+  if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
+  const int ms = max_splits_for(*dims);
+  const SplitPlan plan = plan_splits(m_units(*dims), std::max<int64_t>(1, ceil_div(total_valid, pcp::kTileN)),
+                                     num_sms(), ms);
+  *bytes = ws_layout(*dims, total_valid, plan.splits).total;
+  return PCP_OK;
+}
+
+int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* packed_kv, int32_t num_sources,
+                          const int32_t* valid_len, void* out, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  PCP_TRY(check_dims(dims));
+  const pcp_dims_t& d = *dims;
+  if (!q || !packed_kv || !valid_len || !out || !workspace)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (num_sources <= 0 || num_sources > pcp::kMaxSources)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  const int64_t pay = payload_bytes(d);
+  Part part;
+  for (int s = 0; s < num_sources; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    if (valid_len[s] > 0)
+      part.srcs.push_back({static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+                           valid_len[s], static_cast<int>(part.keys)});
+    part.keys += valid_len[s];
+  }
+  if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  const int sms = num_sms();
+  plan_part(d, &part, sms, max_splits_for(d));
+  const Workspace w = ws_layout(d, part.keys, part.plan.splits);
+  if (workspace_bytes < w.total)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
+  auto* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
+  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+  const bool direct = part.plan.splits == 1;
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
+  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  return PCP_OK;
+}
+
+int pcp_history_attention_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(PCP_ERR_INVALID_ARGUMENT, "workspace is NULL");
+  int err = 0;
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  CUDA_TRY(cudaMemcpy(&err, workspace, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return fail(PCP_ERR_DEVICE_TIMEOUT, "device wait timed out in the attention kernel (code %d)", err);
+  return PCP_OK;
+}
+
+int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void* nccl_unique_id,
+               pcp_handle_t** out) {
+  PCP_TRY(check_dims(dims));
+  if (!out) return fail(PCP_ERR_INVALID_ARGUMENT, "out is NULL");
+  *out = nullptr;
+  const pcp_dims_t& d = *dims;
+  if (rank < 0 || rank >= d.pcp_size) return fail(PCP_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, d.pcp_size);
+  if (d.pcp_size > 1 && !nccl_unique_id) return fail(PCP_ERR_INVALID_ARGUMENT, "pcp_size > 1 needs an NCCL unique id");
+  CUDA_TRY(cudaSetDevice(device));
+  auto* h = new pcp_handle();
+  h->d = d;
+  h->rank = rank;
+  h->device = device;
+  h->sms = num_sms();
+  auto cleanup = [&](int code) {
+    pcp_destroy(h);
+    return code;
+  };
+  const int64_t key_cap = static_cast<int64_t>(d.pcp_size) * d.max_local_blocks * d.block_size;
+  h->w = ws_layout(d, key_cap, max_splits_for(d));
+  if (cudaMalloc(&h->ws, h->w.total) != cudaSuccess)
+    return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu workspace bytes failed", h->w.total));
+  if (cudaMemset(h->ws, 0, h->w.k_off) != cudaSuccess) return cleanup(fail(PCP_ERR_CUDA, "cudaMemset failed"));
+  if (d.pcp_size > 1) {
+    const size_t ring_bytes = static_cast<size_t>(d.pcp_size) * d.max_local_blocks * payload_bytes(d);
+    if (cudaMalloc(&h->ring, ring_bytes) != cudaSuccess)
+      return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu ring bytes failed", ring_bytes));
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    if (cudaStreamCreateWithPriority(&h->comm_stream, cudaStreamNonBlocking, hi) != cudaSuccess)
+      return cleanup(fail(PCP_ERR_CUDA, "stream creation failed"));
+    if (cudaEventCreateWithFlags(&h->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h->ev_comm, cudaEventDisableTiming) != cudaSuccess)
+      return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_unique_id, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&h->comm, d.pcp_size, id, rank, &cfg);
+    const int s = wait_nccl(h->comm, r, 600000);
+    if (s != PCP_OK) {
+      h->comm_failed = true;
+      return cleanup(s);
+    }
+  }
+  for (auto& e : h->pev)
+    if (cudaEventCreate(&e) != cudaSuccess) return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
+  *out = h;
+  return PCP_OK;
+}
+
+int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
+                void* stream) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (h->comm_failed) return fail(PCP_ERR_PEER, "the ring communicator was aborted");
+  return forward_impl(h, q, packed_kv, valid_len, out, static_cast<cudaStream_t>(stream));
+}
+
+int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
+                     void* out_host, void* stream) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (!q_host || !packed_kv_host || !valid_len || !out_host) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  const pcp_dims_t& d = h->d;
+  CUDA_TRY(cudaSetDevice(h->device));
+  const size_t qbytes = static_cast<size_t>(d.num_q_heads) * d.local_q_len * d.head_dim * 2;
+  const size_t kvbytes = static_cast<size_t>(d.max_local_blocks) * payload_bytes(d);
+  if (!h->dq) {
+    CUDA_TRY(cudaMalloc(&h->dq, qbytes));
+    CUDA_TRY(cudaMalloc(&h->dkv, kvbytes));
+    CUDA_TRY(cudaMalloc(&h->dout, qbytes));
+  }
+  const int r = h->rank;
+  if (valid_len[r] < 0 || valid_len[r] > static_cast<int64_t>(d.max_local_blocks) * d.block_size)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d] out of range", r);
+  const size_t live = static_cast<size_t>(ceil_div(valid_len[r], d.block_size)) * payload_bytes(d);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemcpyAsync(h->dq, q_host, qbytes, cudaMemcpyHostToDevice, st));
+  if (live) CUDA_TRY(cudaMemcpyAsync(h->dkv, packed_kv_host, live, cudaMemcpyHostToDevice, st));
+  PCP_TRY(pcp_forward(h, h->dq, h->dkv, valid_len, h->dout, stream));
+  CUDA_TRY(cudaMemcpyAsync(out_host, h->dout, qbytes, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return PCP_OK;
+}
+
+int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  CUDA_TRY(cudaSetDevice(h->device));
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t a = cudaStreamQuery(h->last_stream);
+    cudaError_t b = h->comm_stream ? cudaStreamQuery(h->comm_stream) : cudaSuccess;
+    if (a != cudaSuccess && a != cudaErrorNotReady) return fail(PCP_ERR_CUDA, "stream: %s", cudaGetErrorString(a));
+    if (b != cudaSuccess && b != cudaErrorNotReady) return fail(PCP_ERR_CUDA, "comm stream: %s", cudaGetErrorString(b));
+    if (h->comm) {
+      ncclResult_t st = ncclSuccess;
+      ncclCommGetAsyncError(h->comm, &st);
+      if (st != ncclSuccess && st != ncclInProgress) {
+        ncclCommAbort(h->comm);
+        h->comm = nullptr;
+        h->comm_failed = true;
+        return fail(PCP_ERR_PEER, "NCCL async error: %s", ncclGetErrorString(st));
+      }
+    }
+    if (a == cudaSuccess && b == cudaSuccess) break;
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      if (h->comm) {
+        ncclCommAbort(h->comm);
+        h->comm = nullptr;
+        h->comm_failed = true;
+      }
+      return fail(PCP_ERR_DEVICE_TIMEOUT, "forward not complete after %d ms; ring aborted", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+  int err = 0;
+  CUDA_TRY(cudaMemcpy(&err, h->ws, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return fail(PCP_ERR_DEVICE_TIMEOUT, "device wait timed out in the attention kernel (code %d)", err);
+  return PCP_OK;
+}
+
+int pcp_set_profiling(pcp_handle_t* h, int32_t enable) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  h->profiling = enable != 0;
+  return PCP_OK;
+}
+
+int pcp_get_stats(const pcp_handle_t* hc, pcp_stats_t* out) {
+  if (!hc || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL argument");
+  auto* h = const_cast<pcp_handle_t*>(hc);
+  *out = h->stats;
+  if (!h->profiling) return PCP_OK;
+  CUDA_TRY(cudaSetDevice(h->device));
+  auto span = [&](int slot) -> double {
+    if (!h->pev_used[slot]) return 0.0;
+    float ms = 0.f;
+    if (cudaEventSynchronize(h->pev[2 * slot + 1]) != cudaSuccess) return 0.0;
+    if (cudaEventElapsedTime(&ms, h->pev[2 * slot], h->pev[2 * slot + 1]) != cudaSuccess) return 0.0;
+    return ms;
+  };
+  out->comm_ms = span(0);
+  out->unpack_ms = span(1) + span(3);
+  out->attn_ms = span(2) + span(4);
+  out->combine_ms = span(5);
+  return PCP_OK;
+}
+
+int pcp_destroy(pcp_handle_t* h) {
+  if (!h) return PCP_OK;
+  cudaSetDevice(h->device);
+  if (h->comm) {
+    if (h->comm_failed) {
+      ncclCommAbort(h->comm);
+    } else {
+      ncclResult_t r = ncclCommFinalize(h->comm);
+      wait_nccl(h->comm, r, 60000);
+      ncclCommDestroy(h->comm);
+    }
+    h->comm = nullptr;
+  }
+  if (h->comm_stream) cudaStreamSynchronize(h->comm_stream);
+  for (auto& e : h->pev)
+    if (e) cudaEventDestroy(e);
+  if (h->ev_in) cudaEventDestroy(h->ev_in);
+  if (h->ev_comm) cudaEventDestroy(h->ev_comm);
+  if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
+  cudaFree(h->ring);
+  cudaFree(h->ws);
+  cudaFree(h->dq);
+  cudaFree(h->dkv);
+  cudaFree(h->dout);
+  delete h;
+  return PCP_OK;
+}
+
+int pcp_selftest_bounded_wait(int32_t limit_us, int32_t* device_status) {
+  if (!device_status || limit_us <= 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
+  int* err = nullptr;
+  CUDA_TRY(cudaMalloc(&err, sizeof(int)));
+  cudaMemset(err, 0, sizeof(int));
+  bounded_wait_probe_kernel<<<1, 32>>>(err, static_cast<unsigned long long>(limit_us) * 1000ull);
+  cudaError_t e = cudaDeviceSynchronize();
+  int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(err);
+  if (e != cudaSuccess) return fail(PCP_ERR_CUDA, "probe: %s", cudaGetErrorString(e));
+  *device_status = v;
+  return PCP_OK;
+}
+
+}  // extern "C"

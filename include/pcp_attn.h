@@ -1,0 +1,168 @@
+/*
+ * C ABI of the B200 prefill context-parallel (PCP) history-attention path.
+ *
+ * Replaces the reference's device path (HandsomeHow/aws_training_study):
+ *   pcp_attention/kernel.py:559-564   wrap_for_native_torch(cfg) -> kernel(q, packed_kv, mask)
+ *   pcp_attention/kernel.py:32-556    make_history_attention_kernel(cfg) (the NKI kernel,
+ *                                     with its ring collective_permute at kernel.py:276-293)
+ *   run_poc.py:200-212                root communicator id exchange
+ *   run_poc.py:241-257                host->device copies, compiled call, .cpu()
+ *
+ * Conventions
+ *   - Plain pointers and sizes only; the caller owns every buffer it passes.
+ *   - Device pointers are CUDA device memory of the current device; `stream` is a
+ *     cudaStream_t (NULL = legacy default stream).  Calls are asynchronous on the
+ *     stream unless stated otherwise.
+ *   - Every function returns PCP_OK (0) or a pcp_status code; pcp_last_error()
+ *     gives a message for the calling thread's last failure.
+ *   - Layouts (row-major, innermost last):
+ *       q, out      [num_q_heads][local_q_len][head_dim]                  bf16
+ *       packed_kv   [blocks][2][num_kv_heads][block_size][head_dim]        e4m3fn or bf16
+ *                   (the reference's pack_local_kv ring payload, kernel.py:17-29)
+ *       valid_len   int32 per source rank, host memory: valid history tokens in
+ *                   that rank's shard (its first valid_len tokens; the rest of the
+ *                   blocks is padding and never read).
+ */
+#ifndef PCP_ATTN_H
+#define PCP_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PCP_ATTN_ABI_VERSION 1
+
+enum pcp_kv_dtype {
+  PCP_KV_E4M3 = 0, /* float8_e4m3fn, dequantised at unit scale (reference.py:29-31) */
+  PCP_KV_BF16 = 1
+};
+
+enum pcp_status {
+  PCP_OK = 0,
+  PCP_ERR_INVALID_ARGUMENT = 1,
+  PCP_ERR_UNSUPPORTED = 2,
+  PCP_ERR_CUDA = 3,
+  PCP_ERR_NCCL = 4,
+  PCP_ERR_DEVICE_TIMEOUT = 5,
+  PCP_ERR_OUT_OF_MEMORY = 6,
+  PCP_ERR_PEER = 7
+};
+
+/* Static shape of one PCP rank (the fields of PCPAttentionConfig that fix
+ * buffer shapes, pcp_attention/config.py:17-59). */
+typedef struct pcp_dims {
+  int32_t pcp_size;         /* P: ranks in the ring */
+  int32_t local_q_len;      /* current_len / P */
+  int32_t max_local_blocks; /* cache blocks per rank in packed_kv */
+  int32_t block_size;       /* tokens per cache block */
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;         /* 128 or 256 on the CUDA path */
+  int32_t kv_dtype;         /* enum pcp_kv_dtype */
+} pcp_dims_t;
+
+/* Per-call measurements of the last pcp_forward (device times only when
+ * profiling is enabled; counts always). */
+typedef struct pcp_stats {
+  double attn_ms;          /* summed duration of the attention kernel launches */
+  double unpack_ms;        /* summed duration of the KV unpack launches */
+  double combine_ms;       /* duration of the split combine launch (0 if none) */
+  double comm_ms;          /* ring exchange on the comm stream (0 when P == 1) */
+  int32_t kernel_launches; /* kernels of this library launched by the call */
+  int32_t attn_launches;   /* of which attention kernels */
+  int32_t splits;          /* key splits used (1 = direct bf16 output) */
+  int32_t reserved;
+  int64_t ring_bytes;      /* bytes this rank sent around the ring */
+  int64_t keys;            /* valid history keys attended by this rank */
+} pcp_stats_t;
+
+typedef struct pcp_handle pcp_handle_t;
+
+/* Message for the calling thread's last failing call ("" if none). */
+const char* pcp_last_error(void);
+int pcp_abi_version(void);
+
+/* ---- host-only helpers (no GPU needed) --------------------------------- */
+
+/* Valid history tokens owned by `rank` for a global history of `total_len`
+ * under the striped map of pcp_attention/layout.py:10-16.  Equals the
+ * reference's actual_local_history_len (config.py:45-47) when total_len is a
+ * multiple of pcp_size * interleave_size. */
+int64_t pcp_source_valid_len(int64_t total_len, int32_t pcp_size, int32_t interleave_size, int32_t rank);
+
+/* Ring schedule of hop `hop` (1..P-1) for `rank`: the source rank whose shard
+ * this rank sends to rank+1 and the source rank whose shard it receives from
+ * rank-1 (reference.py:68-71 "source_rank = (rank - step) % P", kernel.py:276-293
+ * receive-from-predecessor permute; the final hop back to the owner is omitted). */
+int pcp_ring_schedule(int32_t rank, int32_t pcp_size, int32_t hop, int32_t* send_source, int32_t* recv_source,
+                      int32_t* send_to, int32_t* recv_from);
+
+/* Bytes of an NCCL unique id, and a fresh one (rank 0 creates, all ranks
+ * receive it out of band; replaces run_poc.py:200-212). */
+int pcp_nccl_unique_id_bytes(void);
+int pcp_get_nccl_unique_id(void* out);
+
+/* ---- stateless single-GPU entry ---------------------------------------- */
+
+/* Device workspace bytes needed by pcp_history_attention for `total_valid`
+ * history keys on the current device. */
+int pcp_history_attention_workspace_size(const pcp_dims_t* dims, int64_t total_valid, size_t* bytes);
+
+/* History attention of one rank whose history is fully resident: the
+ * packed shards of `num_sources` ranks laid out back to back
+ * ([num_sources][max_local_blocks][payload]) with valid_len[num_sources].
+ * For P == 1 this is the whole path (replaces kernel(q, packed_kv, mask) of
+ * kernel.py:559-564 with pcp_size 1).  `workspace` is caller-owned device
+ * memory of pcp_history_attention_workspace_size bytes. */
+int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* packed_kv, int32_t num_sources,
+                          const int32_t* valid_len, void* out, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* Synchronises `stream` and reports a device-side wait timeout recorded in
+ * `workspace` by the last pcp_history_attention on it (PCP_ERR_DEVICE_TIMEOUT). */
+int pcp_history_attention_status(const void* workspace, void* stream);
+
+/* Failure-detection self test: runs one kernel that waits on an mbarrier
+ * nothing arrives at, bounded by limit_us of device time, and returns the
+ * device error word it recorded (199 when the bound fired) in *device_status.
+ * The context stays usable.  Synchronous. */
+int pcp_selftest_bounded_wait(int32_t limit_us, int32_t* device_status);
+
+/* ---- ring entry (one handle per rank) ---------------------------------- */
+
+/* Collective over the P ranks when pcp_size > 1 (every rank calls it with the
+ * same dims and unique id).  `device` is the CUDA device of this rank.  For
+ * pcp_size == 1, nccl_unique_id may be NULL. */
+int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void* nccl_unique_id,
+               pcp_handle_t** out);
+
+/* One forward of this rank: q and packed_kv are this rank's shard (device),
+ * valid_len[P] the valid tokens of every source rank (identical on all ranks),
+ * out the bf16 output (device).  The local shard is attended while the other
+ * shards travel the ring on an internal high-priority stream; `stream` waits
+ * for everything before the call's last kernel writes `out`. */
+int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
+                void* stream);
+
+/* Same, with HOST buffers (pinned or pageable): copies q and packed_kv in,
+ * runs pcp_forward on `stream`, copies out back, and synchronises `stream`. */
+int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
+                     void* out_host, void* stream);
+
+/* Waits up to timeout_ms for the last forward (compute and ring streams) and
+ * reports failures: device-side wait timeouts, CUDA errors, NCCL async errors
+ * (a peer that left).  On a timeout the NCCL communicator is aborted. */
+int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms);
+
+int pcp_set_profiling(pcp_handle_t* h, int32_t enable);
+int pcp_get_stats(const pcp_handle_t* h, pcp_stats_t* out);
+int pcp_destroy(pcp_handle_t* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PCP_ATTN_H */
