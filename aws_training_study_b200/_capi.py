@@ -56,7 +56,7 @@ class PcpStats(ctypes.Structure):
         ("kernel_launches", _I32),
         ("attn_launches", _I32),
         ("splits", _I32),
-        ("reserved", _I32),
+        ("forwards", _I32),
         ("ring_bytes", _c.c_int64),
         ("keys", _c.c_int64),
     ]

@@ -346,11 +346,18 @@ struct pcp_handle {
   void* dq = nullptr;
   void* dkv = nullptr;
   void* dout = nullptr;
+  // Profiling: CUDA event pairs recorded around every launch (on the
+  // stream it is launched on) while profiling is on; resolved lazily.
   bool profiling = false;
-  // profiling events: comm(2) unpackA(2) attnA(2) unpackB(2) attnB(2) combine(2)
-  cudaEvent_t pev[12] = {};
-  bool pev_used[6] = {};
-  pcp_stats_t stats{};
+  struct Span {
+    cudaEvent_t start, end;
+    int slot;  // 0 ring exchange, 1 unpack, 2 attention, 3 combine
+  };
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<Span> spans;
+  pcp_stats_t last{};   // counts of the last forward
+  pcp_stats_t accum{};  // counts accumulated since profiling was enabled
 };
 
 namespace {
@@ -372,10 +379,27 @@ int wait_nccl(ncclComm_t comm, ncclResult_t r, int timeout_ms) {
   return PCP_OK;
 }
 
-void prof_record(pcp_handle* h, int slot, bool end, cudaStream_t st) {
-  if (!h->profiling) return;
-  cudaEventRecord(h->pev[2 * slot + (end ? 1 : 0)], st);
-  h->pev_used[slot] = true;
+cudaEvent_t take_event(pcp_handle* h) {
+  if (h->ev_used == h->ev_pool.size()) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    h->ev_pool.push_back(e);
+  }
+  return h->ev_pool[h->ev_used++];
+}
+
+// Returns the span index (or -1 when profiling is off).
+int prof_begin(pcp_handle* h, int slot, cudaStream_t st) {
+  if (!h->profiling) return -1;
+  cudaEvent_t a = take_event(h), b = take_event(h);
+  if (!a || !b) return -1;
+  cudaEventRecord(a, st);
+  h->spans.push_back({a, b, slot});
+  return static_cast<int>(h->spans.size()) - 1;
+}
+
+void prof_end(pcp_handle* h, int idx, cudaStream_t st) {
+  if (idx >= 0) cudaEventRecord(h->spans[idx].end, st);
 }
 
 int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
@@ -395,7 +419,6 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
   if (total == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
   CUDA_TRY(cudaSetDevice(h->device));
   h->last_stream = st;
-  for (bool& u : h->pev_used) u = false;
   LaunchCounter lc;
   const int64_t pay = payload_bytes(d);
   const int max_splits = h->w.max_splits;
@@ -409,7 +432,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
   if (P > 1) {
     CUDA_TRY(cudaEventRecord(h->ev_in, st));
     CUDA_TRY(cudaStreamWaitEvent(h->comm_stream, h->ev_in, 0));
-    prof_record(h, 0, false, h->comm_stream);
+    const int pc = prof_begin(h, 0, h->comm_stream);
     for (int hop = 1; hop < P; ++hop) {
       const int ssrc = ((r - hop + 1) % P + P) % P;
       const int rsrc = ((r - hop) % P + P) % P;
@@ -428,7 +451,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
                                static_cast<int>(remote.key_off + remote.keys)});
       remote.keys += valid_len[rsrc];
     }
-    prof_record(h, 0, true, h->comm_stream);
+    prof_end(h, pc, h->comm_stream);
     CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
   }
   plan_part(d, &local, h->sms, max_splits);
@@ -448,34 +471,45 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
   CUDA_TRY(cudaMemsetAsync(h->ws, 0, 4, st));
 
   if (local.keys) {
-    prof_record(h, 1, false, st);
+    int sp = prof_begin(h, 1, st);
     PCP_TRY(launch_unpack(d, local.srcs, h->w, h->ws, st, &lc));
-    prof_record(h, 1, true, st);
-    prof_record(h, 2, false, st);
+    prof_end(h, sp, st);
+    sp = prof_begin(h, 2, st);
     PCP_TRY(launch_attention(d, q, h->w, h->ws, local.key_off, local.keys, local.plan, 0, direct, out, st, &lc));
-    prof_record(h, 2, true, st);
+    prof_end(h, sp, st);
   }
   if (P > 1) CUDA_TRY(cudaStreamWaitEvent(st, h->ev_comm, 0));
   if (remote.keys) {
-    prof_record(h, 3, false, st);
+    int sp = prof_begin(h, 1, st);
     PCP_TRY(launch_unpack(d, remote.srcs, h->w, h->ws, st, &lc));
-    prof_record(h, 3, true, st);
-    prof_record(h, 4, false, st);
+    prof_end(h, sp, st);
+    sp = prof_begin(h, 2, st);
     PCP_TRY(launch_attention(d, q, h->w, h->ws, remote.key_off, remote.keys, remote.plan, splits_local, direct, out,
                              st, &lc));
-    prof_record(h, 4, true, st);
+    prof_end(h, sp, st);
   }
   if (!direct) {
-    prof_record(h, 5, false, st);
+    const int sp = prof_begin(h, 3, st);
     PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc));
-    prof_record(h, 5, true, st);
+    prof_end(h, sp, st);
   }
-  h->stats = pcp_stats_t{};
-  h->stats.kernel_launches = lc.kernels;
-  h->stats.attn_launches = lc.attn;
-  h->stats.splits = total_splits;
-  h->stats.ring_bytes = sent;
-  h->stats.keys = total;
+  pcp_stats_t& L = h->last;
+  L = pcp_stats_t{};
+  L.kernel_launches = lc.kernels;
+  L.attn_launches = lc.attn;
+  L.splits = total_splits;
+  L.forwards = 1;
+  L.ring_bytes = sent;
+  L.keys = total;
+  if (h->profiling) {
+    pcp_stats_t& A = h->accum;
+    A.kernel_launches += lc.kernels;
+    A.attn_launches += lc.attn;
+    A.splits = total_splits;
+    A.forwards += 1;
+    A.ring_bytes += sent;
+    A.keys = total;
+  }
   return PCP_OK;
 }
 
@@ -620,8 +654,6 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
       return cleanup(s);
     }
   }
-  for (auto& e : h->pev)
-    if (cudaEventCreate(&e) != cudaSuccess) return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
   *out = h;
   return PCP_OK;
 }
@@ -697,6 +729,14 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms) {
 
 int pcp_set_profiling(pcp_handle_t* h, int32_t enable) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (enable) {
+    // Events still referenced by recorded spans must be complete before reuse.
+    CUDA_TRY(cudaSetDevice(h->device));
+    for (auto& sp : h->spans) cudaEventSynchronize(sp.end);
+    h->spans.clear();
+    h->ev_used = 0;
+    h->accum = pcp_stats_t{};
+  }
   h->profiling = enable != 0;
   return PCP_OK;
 }
@@ -704,20 +744,24 @@ int pcp_set_profiling(pcp_handle_t* h, int32_t enable) {
 int pcp_get_stats(const pcp_handle_t* hc, pcp_stats_t* out) {
   if (!hc || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL argument");
   auto* h = const_cast<pcp_handle_t*>(hc);
-  *out = h->stats;
-  if (!h->profiling) return PCP_OK;
+  if (!h->profiling) {
+    *out = h->last;
+    return PCP_OK;
+  }
   CUDA_TRY(cudaSetDevice(h->device));
-  auto span = [&](int slot) -> double {
-    if (!h->pev_used[slot]) return 0.0;
-    float ms = 0.f;
-    if (cudaEventSynchronize(h->pev[2 * slot + 1]) != cudaSuccess) return 0.0;
-    if (cudaEventElapsedTime(&ms, h->pev[2 * slot], h->pev[2 * slot + 1]) != cudaSuccess) return 0.0;
-    return ms;
-  };
-  out->comm_ms = span(0);
-  out->unpack_ms = span(1) + span(3);
-  out->attn_ms = span(2) + span(4);
-  out->combine_ms = span(5);
+  pcp_stats_t s = h->accum;
+  double ms[4] = {0, 0, 0, 0};
+  for (const auto& sp : h->spans) {
+    float t = 0.f;
+    CUDA_TRY(cudaEventSynchronize(sp.end));
+    CUDA_TRY(cudaEventElapsedTime(&t, sp.start, sp.end));
+    ms[sp.slot] += t;
+  }
+  s.comm_ms = ms[0];
+  s.unpack_ms = ms[1];
+  s.attn_ms = ms[2];
+  s.combine_ms = ms[3];
+  *out = s;
   return PCP_OK;
 }
 
@@ -735,7 +779,8 @@ int pcp_destroy(pcp_handle_t* h) {
     h->comm = nullptr;
   }
   if (h->comm_stream) cudaStreamSynchronize(h->comm_stream);
-  for (auto& e : h->pev)
+  for (auto& sp : h->spans) cudaEventSynchronize(sp.end);
+  for (auto& e : h->ev_pool)
     if (e) cudaEventDestroy(e);
   if (h->ev_in) cudaEventDestroy(h->ev_in);
   if (h->ev_comm) cudaEventDestroy(h->ev_comm);

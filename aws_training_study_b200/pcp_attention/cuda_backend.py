@@ -225,7 +225,7 @@ class HistoryAttention:
     def stats(self) -> dict:
         st = _capi.PcpStats()
         _capi.check(_capi.lib().pcp_get_stats(self._handle, ctypes.byref(st)))
-        return {name: getattr(st, name) for name, _ in _capi.PcpStats._fields_ if name != "reserved"}
+        return {name: getattr(st, name) for name, _ in _capi.PcpStats._fields_}
 
     def close(self) -> None:
         if getattr(self, "_handle", None) is not None and self._handle.value:

@@ -64,19 +64,21 @@ typedef struct pcp_dims {
   int32_t kv_dtype;         /* enum pcp_kv_dtype */
 } pcp_dims_t;
 
-/* Per-call measurements of the last pcp_forward (device times only when
- * profiling is enabled; counts always). */
+/* Measurements accumulated over every pcp_forward since the last
+ * pcp_set_profiling(h, 1) (device times, from CUDA events recorded on the
+ * stream each kernel is launched on).  With profiling off, the counts and
+ * sizes describe the last forward and the times are 0. */
 typedef struct pcp_stats {
   double attn_ms;          /* summed duration of the attention kernel launches */
   double unpack_ms;        /* summed duration of the KV unpack launches */
-  double combine_ms;       /* duration of the split combine launch (0 if none) */
-  double comm_ms;          /* ring exchange on the comm stream (0 when P == 1) */
-  int32_t kernel_launches; /* kernels of this library launched by the call */
+  double combine_ms;       /* summed duration of the split combine launches */
+  double comm_ms;          /* summed ring exchange time on the comm stream */
+  int32_t kernel_launches; /* kernels of this library launched */
   int32_t attn_launches;   /* of which attention kernels */
-  int32_t splits;          /* key splits used (1 = direct bf16 output) */
-  int32_t reserved;
+  int32_t splits;          /* key splits of the last forward (1 = direct bf16 output) */
+  int32_t forwards;        /* forwards accumulated */
   int64_t ring_bytes;      /* bytes this rank sent around the ring */
-  int64_t keys;            /* valid history keys attended by this rank */
+  int64_t keys;            /* valid history keys attended by the last forward */
 } pcp_stats_t;
 
 typedef struct pcp_handle pcp_handle_t;
