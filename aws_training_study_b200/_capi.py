@@ -75,6 +75,7 @@ SIGNATURES = {
     "pcp_history_attention": (_c.c_int, [_PDIMS, _P, _P, _I32, _PI32, _P, _P, _c.c_size_t, _P]),
     "pcp_history_attention_status": (_c.c_int, [_P, _P]),
     "pcp_selftest_bounded_wait": (_c.c_int, [_I32, _PI32]),
+    "pcp_history_attention_noalloc": (_c.c_int, [_PDIMS, _P, _P, _I32, _PI32, _P, _P, _P]),
     "pcp_create": (_c.c_int, [_PDIMS, _I32, _I32, _P, _c.POINTER(_P)]),
     "pcp_forward": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),

@@ -609,6 +609,97 @@ int pcp_history_attention_status(const void* workspace, void* stream) {
   return PCP_OK;
 }
 
+}  // extern "C"
+
+// ----------------------------------------------- allocation-free entry ----
+// Fixed scratch of pcp_history_attention_noalloc: error word, dense bf16 K/V
+// and split partials, laid out exactly as a pcp_history_attention workspace.
+// A static device array, so it exists on every device that loads this
+// library, for the life of the process.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[PCP_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (with that device current).  In host code the symbol is only a
+// host-side stand-in, never a device address, so kernels get this pointer.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(PCP_ERR_UNSUPPORTED, "device %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(PCP_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return PCP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const void* packed_kv, int32_t num_sources,
+                                  const int32_t* valid_len, void* out, int32_t* device_status, void* stream) {
+  PCP_TRY(check_dims(dims));
+  const pcp_dims_t& d = *dims;
+  if (!q || !packed_kv || !valid_len || !out || !device_status)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (num_sources <= 0 || num_sources > pcp::kMaxSources)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  const int64_t pay = payload_bytes(d);
+  Part part;
+  for (int s = 0; s < num_sources; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    if (valid_len[s] > 0)
+      part.srcs.push_back({static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+                           valid_len[s], static_cast<int>(part.keys)});
+    part.keys += valid_len[s];
+  }
+  if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  // The largest split plan whose workspace fits the fixed scratch.
+  const int sms = num_sms();
+  const int64_t n_kt = ceil_div(part.keys, pcp::kTileN);
+  int split_cap = max_splits_for(d);
+  Workspace w;
+  while (true) {
+    part.plan = plan_splits(m_units(d), n_kt, sms, split_cap);
+    w = ws_layout(d, part.keys, part.plan.splits);
+    if (w.total <= PCP_NOALLOC_SCRATCH_BYTES) break;
+    if (part.plan.splits == 1)
+      return fail(PCP_ERR_UNSUPPORTED,
+                  "problem needs %zu scratch bytes; the allocation-free entry has %u (use pcp_history_attention "
+                  "with a caller workspace)",
+                  w.total, PCP_NOALLOC_SCRATCH_BYTES);
+    split_cap = part.plan.splits - 1;
+  }
+  void* scratch = nullptr;
+  PCP_TRY(noalloc_scratch(&scratch));
+  auto* ws = static_cast<uint8_t*>(scratch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The error word is the only scratch state that must start at zero: dense
+  // K/V rows past num_keys are never read (TMA zero-fills past the tensor
+  // map's extent) and every partial the combine reads is rewritten.
+  CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
+  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+  const bool direct = part.plan.splits == 1;
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
+  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  CUDA_TRY(cudaMemcpyAsync(device_status, ws, sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  return PCP_OK;
+}
+
 int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void* nccl_unique_id,
                pcp_handle_t** out) {
   PCP_TRY(check_dims(dims));

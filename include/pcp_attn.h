@@ -133,6 +133,33 @@ int pcp_history_attention_status(const void* workspace, void* stream);
  * The context stays usable.  Synchronous. */
 int pcp_selftest_bounded_wait(int32_t limit_us, int32_t* device_status);
 
+/* ---- allocation-free single-GPU entry ---------------------------------- */
+
+/* No counterpart in the reference: an addition for callers that may not
+ * allocate device memory at all -- code running where cudaMalloc is
+ * forbidden or unsafe (inside a host framework that owns every byte of
+ * device memory, a real-time serving loop that must never hit the allocator,
+ * a plugin whose host forbids allocation).  Same computation and arguments as
+ * pcp_history_attention, but the scratch (error word, dense bf16 K/V, split
+ * partials) lives in a fixed static device array of
+ * PCP_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that loads
+ * the library holds until the process exits.  The caller still passes the
+ * inputs and the output, plus `device_status`: a caller-owned DEVICE int32
+ * that receives the kernel's error word (0, or a wait-timeout code).
+ *   - Problems whose scratch does not fit return PCP_ERR_UNSUPPORTED with the
+ *     size needed; nothing is launched.
+ *   - The call makes no allocation (no cudaMalloc/cudaFree, no library
+ *     allocator).  Its first call on a device looks up the array's device
+ *     address (cudaGetSymbolAddress) with that device current; make that
+ *     first call before any stream capture.
+ *   - Every call on a device shares the one array, which keeps the last
+ *     call's contents (each call clears what must start at zero).  Calls that
+ *     overlap on the GPU (different streams, no ordering between them) race
+ *     on it: order them on one stream or serialise them. */
+#define PCP_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const void* packed_kv, int32_t num_sources,
+                                  const int32_t* valid_len, void* out, int32_t* device_status, void* stream);
+
 /* ---- ring entry (one handle per rank) ---------------------------------- */
 
 /* Collective over the P ranks when pcp_size > 1 (every rank calls it with the
