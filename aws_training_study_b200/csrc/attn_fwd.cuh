@@ -21,9 +21,13 @@
 //   finalise/store (kernel.py:516-553) -> O/l in fp32, bf16 via swizzled smem
 //       + TMA store, or fp32 partial + log2-sum-exp for the split combine.
 //
-// Thread roles (192 threads, 1 CTA per SM):
-//   warps 0-3 softmax / correction / epilogue, warp 4 TMA producer,
-//   warp 5 TMEM allocator and single-thread MMA issuer.
+// Thread roles (320 threads, 1 CTA per SM):
+//   warps 0-7 softmax / correction / epilogue in two warpgroups: warpgroup w
+//     owns key columns [64w, 64w+64) of every S tile and head-dim columns
+//     [w*D/2, (w+1)*D/2) of O; the two exchange their partial row max through
+//     shared memory once per tile, which halves the per-tile latency of the
+//     softmax that sits between the QK^T and PV MMAs,
+//   warp 8 TMA producer, warp 9 TMEM allocator and single-thread MMA issuer.
 #pragma once
 
 #include <cuda.h>
@@ -41,6 +45,11 @@ constexpr int kStageBytes = 2 * kBoxBytes;  // [128 keys, 128 dims] bf16
 constexpr int kTmemCols = 512;
 constexpr int kTmemS0 = 256;      // S/P buffers at columns 256 and 384; O at 0
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kSoftmaxWarpgroups = 2;
+constexpr int kSoftmaxThreads = 128 * kSoftmaxWarpgroups;
+constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
+constexpr int kProducerWarp = kSoftmaxThreads / 32;
+constexpr int kMmaWarp = kProducerWarp + 1;
 
 enum : int {
   kErrWaitQ = 101,
@@ -49,6 +58,8 @@ enum : int {
   kErrWaitPFull = 104,
   kErrWaitSFull = 105,
   kErrWaitODone = 106,
+  kErrSmemAlign = 107,
+  kErrWaitRed = 108,
 };
 
 struct AttnParams {
@@ -74,15 +85,21 @@ struct AttnSmem {
   static constexpr int kQOff = 0;
   static constexpr int kStageOff = kQBytes;
   static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
-  // barriers: q_full, kv_full[NS], kv_empty[NS], s_full[2], p_full[2], o_done, teardown
-  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1 + 1;
+  // barriers: q_full, kv_full[NS], kv_empty[NS], s_full[2], p_full[2], o_done,
+  // teardown, red[2] (row-max exchange between the softmax warpgroups)
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1 + 1 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kBytes = kMiscOff + 16;
-  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+  // Row-max exchange between the softmax warpgroups: [tile parity][wg][row].
+  static constexpr int kRedOff = kMiscOff + 16;
+  static constexpr int kBytes = kRedOff + 2 * kSoftmaxWarpgroups * kTileM * 4;
+  // The dynamic smem base is declared 1024-aligned (128B-swizzle atoms); the
+  // kernel verifies it and reports an error instead of running misaligned.
+  static constexpr int kAlloc = kBytes;
+  static_assert(kAlloc <= 232448, "exceeds the 227 KB of shared memory per CTA");
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                     const AttnParams p) {
@@ -90,9 +107,12 @@ __global__ void __launch_bounds__(192, 1)
   constexpr int NS = L::kStages;
   constexpr int NH = L::kHalves;
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {  // uniform across the CTA: nothing has started yet
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrSmemAlign);
+    return;
+  }
   const uint32_t sQ = sbase + L::kQOff;
   const uint32_t sStage = sbase + L::kStageOff;
   const uint32_t bars = sbase + L::kBarOff;
@@ -103,8 +123,10 @@ __global__ void __launch_bounds__(192, 1)
   auto bar_p_full = [&](int b) { return bars + 8u * (3 + 2 * NS + b); };
   const uint32_t bar_o = bars + 8u * (5 + 2 * NS);
   const uint32_t bar_td = bars + 8u * (6 + 2 * NS);
+  auto bar_red = [&](int b) { return bars + 8u * (7 + 2 * NS + b); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -117,7 +139,7 @@ __global__ void __launch_bounds__(192, 1)
   const int kt1 = min(kt0 + p.tiles_per_split, n_key_tiles);
   const int n = kt1 - kt0;  // >= 1 by construction on the host
 
-  if (warp == 4 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_kv_full(s), 1);
@@ -125,14 +147,16 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_s_full(b), 1);
-      mbar_init(bar_p_full(b), kTileM);
+      mbar_init(bar_p_full(b), kSoftmaxThreads);
     }
     mbar_init(bar_o, 1);
     mbar_init(bar_td, 1);
+    mbar_init(bar_red(0), kSoftmaxThreads);
+    mbar_init(bar_red(1), kSoftmaxThreads);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -141,7 +165,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------ TMA producer --
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm_q);
@@ -177,7 +201,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // -------------------------------------------------------- MMA issuer --
     if (lane == 0 && n > 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kTileM, kTileN, false, false);
@@ -241,11 +265,18 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ---------------------------------------- softmax / correction / epilogue --
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // Thread = query row (TMEM lane); warpgroup `wg` owns S key columns
+    // [64 wg, 64 wg + 64) and O columns [wg D/2, (wg+1) D/2).  Both warpgroups
+    // keep identical running maxima (they combine the same tile max), and
+    // each keeps a partial row sum over its own columns.
+    constexpr int kHalfKeys = kTileN / kSoftmaxWarpgroups;  // 64
+    constexpr int kOCols = D / kSoftmaxWarpgroups;          // 128 or 64
+    const int wg = warp >> 2;
+    const int row = threadIdx.x & (kTileM - 1);  // == TMEM lane
+    const uint32_t t_row = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sl2 = p.scale_log2;
     float m_ref = -INFINITY;  // raw-score running reference max
-    float l = 0.f;
+    float l = 0.f;            // partial row sum over this warpgroup's columns
     bool ok = n > 0;
     // Every wait result is made warp-uniform (__all_sync) so that the
     // warp-collective tcgen05.ld/st below never run with part of a warp.
@@ -254,25 +285,35 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1u, abort_flag, p.err, kErrWaitSFull));
       if (!ok) break;
       tc_fence_after();
-      float s[kTileN];
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(t_row + kTmemS0 + b * kTileN + c4 * 32, s + c4 * 32);
+      const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
+      float s[kHalfKeys];
+      tmem_ld32(t_s + wg * kHalfKeys, s);
+      tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
       tmem_wait_ld();
-      const int valid = p.num_keys - (kt0 + j) * kTileN;
-      if (valid < kTileN) {
+      const int valid = p.num_keys - (kt0 + j) * kTileN - wg * kHalfKeys;
+      if (valid < kHalfKeys) {
 #pragma unroll
-        for (int i = 0; i < kTileN; ++i)
+        for (int i = 0; i < kHalfKeys; ++i)
           if (i >= valid) s[i] = -INFINITY;
       }
       float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-      for (int i = 4; i < kTileN; i += 4) {
+      for (int i = 4; i < kHalfKeys; i += 4) {
         mx0 = fmaxf(mx0, s[i]);
         mx1 = fmaxf(mx1, s[i + 1]);
         mx2 = fmaxf(mx2, s[i + 2]);
         mx3 = fmaxf(mx3, s[i + 3]);
       }
-      const float tmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      // Exchange partial maxima through smem, double-buffered by tile parity
+      // (a warpgroup can be at most one tile ahead of the other), with a
+      // bounded mbarrier wait.  After it both warpgroups have finished
+      // reading S_j, so the P stores below may overwrite any of its columns.
+      red[(b * kSoftmaxWarpgroups + wg) * kTileM + row] = pmax;
+      mbar_arrive(bar_red(b));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_red(b), (j >> 1) & 1u, abort_flag, p.err, kErrWaitRed));
+      if (!ok) break;
+      const float tmax = fmaxf(pmax, red[(b * kSoftmaxWarpgroups + (wg ^ 1)) * kTileM + row]);
       const bool need = (tmax - m_ref) * sl2 > kRescaleThreshold;
       float alpha = 1.f;
       if (need) {
@@ -283,17 +324,19 @@ __global__ void __launch_bounds__(192, 1)
       const float neg = -m_ref * sl2;
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < kHalfKeys / 32; ++c2) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(s[c4 * 32 + 2 * i], sl2, neg));
-          const float p1 = ex2_approx(fmaf(s[c4 * 32 + 2 * i + 1], sl2, neg));
+          const float p0 = ex2_approx(fmaf(s[c2 * 32 + 2 * i], sl2, neg));
+          const float p1 = ex2_approx(fmaf(s[c2 * 32 + 2 * i + 1], sl2, neg));
           sum0 += p0;
           sum1 += p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(t_row + kTmemS0 + b * kTileN + c4 * 16, pk);
+        // P (bf16 pairs) of keys [64 wg + 32 c2, +32) -> TMEM columns
+        // [32 wg + 16 c2, +16) of the S buffer: the PV MMA's A operand.
+        tmem_st16(t_s + wg * (kHalfKeys / 2) + c2 * 16, pk);
       }
       tmem_wait_st();
       l += sum0 + sum1;
@@ -305,13 +348,14 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < kOCols / 32; ++c) {
             float o[32];
-            tmem_ld32(t_row + c * 32, o);
+            const uint32_t t_o = t_row + wg * kOCols + c * 32;
+            tmem_ld32(t_o, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(t_row + c * 32, o);
+            tmem_st32(t_o, o);
           }
           tmem_wait_st();
         }
@@ -320,35 +364,41 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(bar_p_full(b));
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (n - 1) & 1u, abort_flag, p.err, kErrWaitODone));
-    // All 128 softmax threads reach this barrier (every wait above is
-    // bounded); after it the epilogue decision is uniform across them.
-    ok = named_bar_and(1, kTileM, ok && (*abort_flag == 0));
+    // All softmax threads reach this barrier (every wait above is bounded);
+    // after it the epilogue decision is uniform across them, and no thread
+    // still reads the row-max exchange buffer.
+    ok = named_bar_and(1, kSoftmaxThreads, ok && (*abort_flag == 0));
     if (ok) {
       tc_fence_after();
-      const float inv_l = 1.f / l;
+      red[wg * kTileM + row] = l;
+      named_bar_sync(2, kSoftmaxThreads);
+      const float l_tot = l + red[(wg ^ 1) * kTileM + row];
+      const float inv_l = 1.f / l_tot;
       if (p.write_final) {
         // bf16 O -> Q's smem (all MMAs are complete) in the 128B-swizzled box
         // layout the O tensor map expects, then one thread issues TMA stores.
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kOCols / 32; ++c) {
           float o[32];
-          tmem_ld32(t_row + c * 32, o);
+          const int col = wg * kOCols + c * 32;
+          tmem_ld32(t_row + col, o);
           tmem_wait_ld();
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
-          const int box = c >> 1;
+          const int box = col / kBoxCols;
           uint8_t* rowp = smem + L::kQOff + box * kBoxBytes + row * 128;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const int chunk = (c & 1) * 4 + q;
+            const int chunk = ((col % kBoxCols) / 8) + q;
             const int phys = chunk ^ (row & 7);
-            *reinterpret_cast<uint4*>(rowp + phys * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            *reinterpret_cast<uint4*>(rowp + phys * 16) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
           }
         }
         fence_proxy_async_smem();
-        named_bar_sync(3, kTileM);
-        if (row == 0) {
+        named_bar_sync(3, kSoftmaxThreads);
+        if (threadIdx.x == 0) {
           for (int box = 0; box < D / kBoxCols; ++box)
             tma_store_3d(&tm_o, sQ + box * kBoxBytes, box * kBoxCols, mt * kTileM, head);
           tma_store_commit();
@@ -358,12 +408,12 @@ __global__ void __launch_bounds__(192, 1)
         const int rih = mt * kTileM + row;
         const size_t split_idx = static_cast<size_t>(p.split_base + split);
         const size_t grow = static_cast<size_t>(head) * p.rows_per_head + rih;
-        float* dst = p.part_o + (split_idx * p.total_rows + grow) * D;
+        float* dst = p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols;
         const bool live = rih < p.rows_per_head;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kOCols / 32; ++c) {
           float o[32];
-          tmem_ld32(t_row + c * 32, o);
+          tmem_ld32(t_row + wg * kOCols + c * 32, o);
           tmem_wait_ld();
           if (live) {
 #pragma unroll
@@ -372,14 +422,14 @@ __global__ void __launch_bounds__(192, 1)
                   make_float4(o[i] * inv_l, o[i + 1] * inv_l, o[i + 2] * inv_l, o[i + 3] * inv_l);
           }
         }
-        if (live) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l);
+        if (live && wg == 0) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }

@@ -1,0 +1,423 @@
+// History-attention forward on CTA pairs (tcgen05 cta_group::2).
+//
+// Same computation, stages and numerics as attn_fwd_kernel (see that file's
+// header for the map to the reference's NKI kernel, pcp_attention/kernel.py:
+// 84-554), but every work unit is a cluster of two CTAs on two SMs that
+// share one 256-row MMA:
+//   * CTA r of the pair owns query rows [256 t + 128 r, +128) of one KV head:
+//     its Q rows in its smem, its S/P and O rows in its TMEM.
+//   * QK^T: S[256, 128 keys] = Q K^T with B = K split by keys: CTA r holds
+//     keys [64 r, 64 r + 64) of the tile ([64 keys, D] in smem).
+//   * PV:   O[256, D] += P V with B = V split by head dim: CTA r holds
+//     V[128 keys, D/2 * r .. +D/2] (MN-major).  A = P from each CTA's TMEM.
+//   * The leader (rank 0) issues every MMA; completion is multicast to both
+//     CTAs' mbarriers.  Both CTAs' TMA loads count their bytes on the
+//     leader's barriers; both softmax warpgroups arrive on the leader's P
+//     barrier (one arrive per warp).
+// Per CTA and 128-key tile this moves 64 KB of K/V through TMA instead of
+// 128 KB, and the tensor cores read 96 KB + 32 KB of smem operands instead
+// of 128 KB + 64 KB, so the smem ring holds 2.5 tiles of look-ahead.
+// No TMA multicast is used: each CTA loads only its own smem.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "attn_fwd.cuh"
+#include "ptx.cuh"
+
+namespace pcp {
+
+template <int D>
+struct PairSmem {
+  static constexpr int kQBytes = D * 2 * kTileM;           // own 128 rows (D/64 boxes of 16 KB)
+  static constexpr int kStageBytes = 128 * D;              // K half [64, D] or V half [128, D/2], bf16
+  static constexpr int kKBox = 64 * 128;                   // K box: 64 rows x 128 B
+  static constexpr int kVBox = 128 * 128;                  // V box: 128 rows x 128 B
+  static constexpr int kStages = (D == 256) ? 5 : 12;
+  static constexpr int kQOff = 0;
+  static constexpr int kStageOff = kQBytes;
+  static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
+  // q_full, kv_full[NS], kv_empty[NS], s_full[2], p_full[2], o_done[2], teardown, red[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 2;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kRedOff = kMiscOff + 16;
+  static constexpr int kBytes = kRedOff + 2 * kSoftmaxWarpgroups * kTileM * 4;
+  static constexpr int kAlloc = kBytes;
+  static_assert(kAlloc <= 232448, "exceeds the 227 KB of shared memory per CTA");
+};
+
+constexpr int kPairRows = 2 * kTileM;
+constexpr uint16_t kBothCtas = 0x3;
+constexpr uint16_t kLeaderCta = 0x1;
+constexpr int kSoftmaxWarps = kSoftmaxThreads / 32;
+
+// p.m_tiles_per_head counts 256-row pair tiles here.
+template <int D>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    attn_fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                         const AttnParams p) {
+  using L = PairSmem<D>;
+  constexpr int NS = L::kStages;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {  // identical in both CTAs: neither starts
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrSmemAlign);
+    return;
+  }
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t sQ = sbase + L::kQOff;
+  const uint32_t sStage = sbase + L::kStageOff;
+  const uint32_t bars = sbase + L::kBarOff;
+  const uint32_t bar_q = bars;
+  auto bar_kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto bar_kv_empty = [&](int s) { return bars + 8u * (1 + NS + s); };
+  auto bar_s_full = [&](int b) { return bars + 8u * (1 + 2 * NS + b); };
+  auto bar_p_full = [&](int b) { return bars + 8u * (3 + 2 * NS + b); };
+  // o_done[b] completes once per PV_j with j % 2 == b (phase j / 2).
+  auto bar_o = [&](int b) { return bars + 8u * (5 + 2 * NS + b); };
+  const uint32_t bar_td = bars + 8u * (7 + 2 * NS);
+  auto bar_red = [&](int b) { return bars + 8u * (8 + 2 * NS + b); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x >> 1;
+  const int head = pair / p.m_tiles_per_head;
+  const int pt = pair % p.m_tiles_per_head;
+  const int row0 = pt * kPairRows + static_cast<int>(rank) * kTileM;  // first query row of this CTA
+  const int split = blockIdx.y;
+  const int n_key_tiles = (p.num_keys + kTileN - 1) / kTileN;
+  const int kt0 = split * p.tiles_per_split;
+  const int kt1 = min(kt0 + p.tiles_per_split, n_key_tiles);
+  const int n = kt1 - kt0;  // >= 1 by construction on the host
+
+  if (warp == kProducerWarp && lane == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar_kv_full(s), 1);
+      mbar_init(bar_kv_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_s_full(b), 1);
+      mbar_init(bar_p_full(b), 2 * kSoftmaxWarps);  // one arrive per softmax warp of both CTAs
+    }
+    mbar_init(bar_o(0), 1);
+    mbar_init(bar_o(1), 1);
+    mbar_init(bar_td, 1);
+    mbar_init(bar_red(0), kSoftmaxThreads);
+    mbar_init(bar_red(1), kSoftmaxThreads);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      if (leader) mbar_arrive_expect_tx(bar_q, 2 * L::kQBytes);
+      const uint32_t q_lead = mapa_shared(bar_q, 0);
+      for (int b = 0; b < D / kBoxCols; ++b)
+        tma_load_3d_pair(sQ + b * kBoxBytes, &tm_q, b * kBoxCols, row0, head, q_lead);
+      uint32_t c = 0;
+      bool ok = true;
+      // Item order = MMA consumption order: K_0, then (K_{j+1}, V_j) per tile.
+      auto issue = [&](bool is_v, int kt) {
+        const int st = c % NS;
+        if (!mbar_wait(bar_kv_empty(st), ((c / NS) & 1u) ^ 1u, abort_flag, p.err, kErrWaitKvEmpty)) return false;
+        if (leader) mbar_arrive_expect_tx(bar_kv_full(st), 2 * L::kStageBytes);
+        const uint32_t full_lead = mapa_shared(bar_kv_full(st), 0);
+        const uint32_t dst = sStage + st * L::kStageBytes;
+        if (!is_v) {
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d_pair(dst + b * L::kKBox, &tm_k, b * kBoxCols, kt * kTileN + static_cast<int>(rank) * 64,
+                             head, full_lead);
+        } else {
+          for (int b = 0; b < D / 2 / kBoxCols; ++b)
+            tma_load_3d_pair(dst + b * L::kVBox, &tm_v, static_cast<int>(rank) * (D / 2) + b * kBoxCols,
+                             kt * kTileN, head, full_lead);
+        }
+        ++c;
+        return true;
+      };
+      ok = issue(false, kt0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) ok = issue(false, kt0 + j + 1);
+        if (ok) ok = issue(true, kt0 + j);
+      }
+      if (!ok) {
+        // Abort: let copies already in flight land before the CTA exits.
+        if (leader) {
+          for (uint32_t i = (c > (uint32_t)NS ? c - NS : 0); i < c; ++i)
+            mbar_wait_teardown(bar_kv_full(i % NS), (i / NS) & 1u);
+          mbar_wait_teardown(bar_q, 0);
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // --------------------------------------------- MMA issuer (leader only) --
+    if (leader && lane == 0 && n > 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(kPairRows, kTileN, false, false);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kPairRows, D, false, true);
+      uint32_t c = 0;
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.err, kErrWaitQ);
+      tc_fence_after();
+      auto qk = [&](int j) {
+        const uint32_t s_tmem = tmem + kTmemS0 + (j & 1) * kTileN;
+        const int st = c % NS;
+        if (!mbar_wait(bar_kv_full(st), (c / NS) & 1u, abort_flag, p.err, kErrWaitKvFull)) return false;
+        tc_fence_after();
+        const uint32_t kbase = sStage + st * L::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t qa = sQ + (kk / 4) * kBoxBytes + (kk % 4) * 32;
+          const uint32_t kb = kbase + (kk / 4) * L::kKBox + (kk % 4) * 32;
+          umma_ss_pair(s_tmem, make_sw128_desc(qa, 16, 1024), make_sw128_desc(kb, 16, 1024), idesc_qk,
+                       kk != 0 ? 1u : 0u);
+        }
+        umma_commit_pair(bar_kv_empty(st), kBothCtas);
+        ++c;
+        umma_commit_pair(bar_s_full(j & 1), kBothCtas);
+        return true;
+      };
+      auto pv = [&](int j) {
+        if (!mbar_wait(bar_p_full(j & 1), (j >> 1) & 1u, abort_flag, p.err, kErrWaitPFull)) return false;
+        const int st = c % NS;
+        if (!mbar_wait(bar_kv_full(st), (c / NS) & 1u, abort_flag, p.err, kErrWaitKvFull)) return false;
+        tc_fence_after();
+        const uint32_t p_tmem = tmem + kTmemS0 + (j & 1) * kTileN;
+        const uint32_t vbase = sStage + st * L::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTileN / 16; ++kk) {
+          // A = P: keys [0, 64) sit in TMEM columns [0, 32) of the S buffer and
+          // keys [64, 128) in columns [64, 96) (each softmax warpgroup writes
+          // inside its own S columns); 16 keys = 8 columns per step.
+          // B = V half, MN-major: 64-dim chunks 16 KB apart (LBO), 8-key
+          // groups 1 KB apart (SBO); a 16-key step is 2 KB.
+          const uint32_t a_cols = kk * 8 + (kk >= 4 ? 32 : 0);
+          umma_ts_pair(tmem, p_tmem + a_cols, make_sw128_desc(vbase + kk * 2048, L::kVBox, 1024), idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit_pair(bar_kv_empty(st), kBothCtas);
+        ++c;
+        umma_commit_pair(bar_o(j & 1), kBothCtas);
+        return true;
+      };
+      if (ok) ok = qk(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) ok = qk(j + 1);
+        if (ok) ok = pv(j);
+      }
+      // Drain: completes when every MMA issued above has.
+      umma_commit_pair(bar_td, kLeaderCta);
+      mbar_wait_teardown(bar_td, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------- softmax / correction / epilogue --
+    constexpr int kHalfKeys = kTileN / kSoftmaxWarpgroups;  // 64
+    constexpr int kOCols = D / kSoftmaxWarpgroups;
+    const int wg = warp >> 2;
+    const int row = threadIdx.x & (kTileM - 1);  // == TMEM lane
+    const uint32_t t_row = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    bool ok = n > 0;
+    // P_j = 2^((s - m_ref) * scale * log2 e) for this warpgroup's 64 keys:
+    // three of every four pairs on the MUFU (ex2.approx), one on the FMA pipe
+    // (exp2_poly), so the 16K exponentials of a tile are not all serialised
+    // on the 16-lane/clk MUFU.  Stores P (bf16) over the S columns and
+    // returns the fp32 sum.
+    auto make_p = [&](const float* sv, float m, uint32_t t_s) {
+      const float neg = -m * sl2;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int c2 = 0; c2 < kHalfKeys / 32; ++c2) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = fmaf(sv[c2 * 32 + 2 * i], sl2, neg);
+          const float x1 = fmaf(sv[c2 * 32 + 2 * i + 1], sl2, neg);
+          const float p0 = (i & 3) == 3 ? exp2_poly(x0) : ex2_approx(x0);
+          const float p1 = (i & 3) == 3 ? exp2_poly(x1) : ex2_approx(x1);
+          sum0 += p0;
+          sum1 += p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        // P of keys [64 wg + 32 c2, +32) as bf16 pairs -> TMEM columns
+        // [64 wg + 16 c2, +16): inside this warpgroup's own S columns, so the
+        // stores never touch S values the other warpgroup has yet to read.
+        tmem_st16(t_s + wg * kHalfKeys + c2 * 16, pk);
+      }
+      tmem_wait_st();
+      return sum0 + sum1;
+    };
+    for (int j = 0; j < n && ok; ++j) {
+      const int b = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1u, abort_flag, p.err, kErrWaitSFull));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
+      float s[kHalfKeys];
+      tmem_ld32(t_s + wg * kHalfKeys, s);
+      tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
+      tmem_wait_ld();
+      const int valid = p.num_keys - (kt0 + j) * kTileN - wg * kHalfKeys;
+      if (valid < kHalfKeys) {
+#pragma unroll
+        for (int i = 0; i < kHalfKeys; ++i)
+          if (i >= valid) s[i] = -INFINITY;
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int i = 4; i < kHalfKeys; i += 4) {
+        mx0 = fmaxf(mx0, s[i]);
+        mx1 = fmaxf(mx1, s[i + 1]);
+        mx2 = fmaxf(mx2, s[i + 2]);
+        mx3 = fmaxf(mx3, s[i + 3]);
+      }
+      const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      // Publish this half's max (double-buffered by tile parity; a
+      // warpgroup is at most one tile ahead of the other).
+      red[(b * kSoftmaxWarpgroups + wg) * kTileM + row] = pmax;
+      mbar_arrive(bar_red(b));
+      // Tiles after the first: compute P with the current reference max
+      // before the other half's max is known -- it only matters when the
+      // row max moved by more than the rescale threshold, which is rare.
+      float tile_sum = 0.f;
+      if (j > 0) tile_sum = make_p(s, m_ref, t_s);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_red(b), (j >> 1) & 1u, abort_flag, p.err, kErrWaitRed));
+      if (!ok) break;
+      const float tmax = fmaxf(pmax, red[(b * kSoftmaxWarpgroups + (wg ^ 1)) * kTileM + row]);
+      const bool need = (tmax - m_ref) * sl2 > kRescaleThreshold;  // always true on the first tile
+      const bool redo = __any_sync(0xffffffffu, need);
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx((m_ref - tmax) * sl2);  // 0 on the first tile
+        m_ref = tmax;
+        l *= alpha;
+      }
+      if (redo) tile_sum = make_p(s, m_ref, t_s);
+      l += tile_sum;
+      // O is rescaled only when the reference max moved (rare): then PV_{j-1}
+      // must be complete first.  Otherwise P_j is released at once, so the
+      // MMA warp can issue PV_j without waiting for PV_{j-1} to finish.
+      // (s_full[j] already implies PV_{j-2} is complete: QK_j was issued
+      // after it, and tcgen05 MMAs complete in issue order.)
+      if (j > 0 && redo) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(bar_o((j - 1) & 1), ((j - 1) >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kOCols / 32; ++c) {
+          float o[32];
+          const uint32_t t_o = t_row + wg * kOCols + c * 32;
+          tmem_ld32(t_o, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_o, o);
+        }
+        tmem_wait_st();
+      }
+      // One arrive per warp on the leader's P barrier (all lanes' TMEM stores
+      // are complete: tcgen05.wait::st is warp-collective).
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(bar_p_full(b), 0));
+    }
+    if (ok)
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(bar_o((n - 1) & 1), ((n - 1) >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
+    ok = named_bar_and(1, kSoftmaxThreads, ok && (*abort_flag == 0));
+    if (ok) {
+      tc_fence_after();
+      red[wg * kTileM + row] = l;
+      named_bar_sync(2, kSoftmaxThreads);
+      const float l_tot = l + red[(wg ^ 1) * kTileM + row];
+      const float inv_l = 1.f / l_tot;
+      if (p.write_final) {
+#pragma unroll 1
+        for (int c = 0; c < kOCols / 32; ++c) {
+          float o[32];
+          const int col = wg * kOCols + c * 32;
+          tmem_ld32(t_row + col, o);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
+          const int box = col / kBoxCols;
+          uint8_t* rowp = smem + L::kQOff + box * kBoxBytes + row * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = ((col % kBoxCols) / 8) + q;
+            const int phys = chunk ^ (row & 7);
+            *reinterpret_cast<uint4*>(rowp + phys * 16) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(3, kSoftmaxThreads);
+        if (threadIdx.x == 0 && row0 < p.rows_per_head) {  // no store of a tile wholly past the rows
+          for (int box = 0; box < D / kBoxCols; ++box)
+            tma_store_3d(&tm_o, sQ + box * kBoxBytes, box * kBoxCols, row0, head);
+          tma_store_commit();
+          tma_store_wait0();
+        }
+      } else {
+        const int rih = row0 + row;
+        const size_t split_idx = static_cast<size_t>(p.split_base + split);
+        const size_t grow = static_cast<size_t>(head) * p.rows_per_head + rih;
+        float* dst = p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols;
+        const bool live = rih < p.rows_per_head;
+#pragma unroll 1
+        for (int c = 0; c < kOCols / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_row + wg * kOCols + c * 32, o);
+          tmem_wait_ld();
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + c * 32 + i) =
+                  make_float4(o[i] * inv_l, o[i + 1] * inv_l, o[i + 2] * inv_l, o[i + 3] * inv_l);
+          }
+        }
+        if (live && wg == 0) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
+      }
+    }
+  }
+
+  // Both CTAs: the leader's MMAs (which read the peer's smem and TMEM) are
+  // drained, every TMEM read and TMA store of either CTA is done.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+}  // namespace pcp

@@ -19,7 +19,7 @@
 #include <thread>
 #include <vector>
 
-#include "attn_fwd.cuh"
+#include "attn_pair.cuh"
 #include "kv_stage.cuh"
 
 namespace {
@@ -66,15 +66,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // bf16 tensor [heads][rows][cols] (cols contiguous, heads `head_stride` elements
-// apart), boxes of 64 cols x 128 rows x 1 head with 128-byte swizzle.
+// apart), boxes of 64 cols x `box_rows` rows x 1 head with 128-byte swizzle.
 int make_tmap(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint64_t heads,
-              uint64_t head_stride) {
+              uint64_t head_stride, uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (!fn) return fail(PCP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
   if (reinterpret_cast<uintptr_t>(base) % 16) return fail(PCP_ERR_INVALID_ARGUMENT, "TMA base not 16-byte aligned");
   cuuint64_t dims[3] = {cols, rows, heads};
   cuuint64_t strides[2] = {cols * 2, head_stride * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -93,9 +93,11 @@ struct SplitPlan {
 };
 
 // Choose how many key splits a launch uses so that (work units) fill whole
-// waves of the SMs.  Cost model: waves * (tiles per unit + 2 tiles of fixed
-// prologue/epilogue cost), with a small bias against splitting.
+// waves of the SMs.  A work unit is a CTA pair (two SMs).  Cost model:
+// waves * (tiles per unit + 2 tiles of fixed prologue/epilogue cost), with a
+// small bias against splitting.
 SplitPlan plan_splits(int64_t m_units, int64_t n_kt, int sms, int max_splits) {
+  const int64_t slots = std::max(1, sms / 2);
   SplitPlan best;
   best.splits = 1;
   best.tiles_per_split = static_cast<int>(n_kt);
@@ -104,7 +106,7 @@ SplitPlan plan_splits(int64_t m_units, int64_t n_kt, int sms, int max_splits) {
   for (int s = 1; s <= smax; ++s) {
     const int64_t tps = ceil_div(n_kt, s);
     const int64_t s_eff = ceil_div(n_kt, tps);
-    const int64_t waves = ceil_div(m_units * s_eff, sms);
+    const int64_t waves = ceil_div(m_units * s_eff, slots);
     const double cost = static_cast<double>(waves) * (static_cast<double>(tps) + 2.0) + (s_eff > 1 ? 0.5 : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
@@ -137,7 +139,8 @@ int64_t payload_bytes(const pcp_dims_t& d) {
 }
 int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads / d.num_kv_heads) * d.local_q_len; }
 int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
-int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kTileM); }
+// Work units of one split: 256-row CTA-pair tiles over every KV head.
+int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kPairRows); }
 
 int num_sms() {
   int dev = 0, sms = 148;
@@ -182,8 +185,8 @@ int set_smem_attr() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(done & (1 << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(pcp::attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pcp::AttnSmem<D>::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(pcp::attn_fwd_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pcp::PairSmem<D>::kAlloc);
     if (e != cudaSuccess) return fail(PCP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done |= (1 << dev);
   }
@@ -231,12 +234,12 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
                      int64_t num_keys, const SplitPlan& plan, int split_base, bool final_out, void* out,
                      cudaStream_t st, LaunchCounter* lc) {
   const int64_t R = rows_per_head(d);
-  const int64_t mt = ceil_div(R, pcp::kTileM);
+  const int64_t mt = ceil_div(R, pcp::kPairRows);  // CTA-pair tiles per KV head
   CUtensorMap tq, tk, tv, to;
   const auto* kb = reinterpret_cast<const __nv_bfloat16*>(ws + w.k_off) + key_off * d.head_dim;
   const auto* vb = reinterpret_cast<const __nv_bfloat16*>(ws + w.v_off) + key_off * d.head_dim;
   PCP_TRY(make_tmap(&tq, q, d.head_dim, R, d.num_kv_heads, R * d.head_dim));
-  PCP_TRY(make_tmap(&tk, kb, d.head_dim, num_keys, d.num_kv_heads, w.key_stride * d.head_dim));
+  PCP_TRY(make_tmap(&tk, kb, d.head_dim, num_keys, d.num_kv_heads, w.key_stride * d.head_dim, 64));
   PCP_TRY(make_tmap(&tv, vb, d.head_dim, num_keys, d.num_kv_heads, w.key_stride * d.head_dim));
   PCP_TRY(make_tmap(&to, final_out ? out : q, d.head_dim, R, d.num_kv_heads, R * d.head_dim));
   pcp::AttnParams p{};
@@ -252,13 +255,14 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   p.part_o = reinterpret_cast<float*>(ws + w.po_off);
   p.part_lse = reinterpret_cast<float*>(ws + w.pl_off);
   p.err = reinterpret_cast<int*>(ws);
-  dim3 grid(static_cast<unsigned>(d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
+  // Two CTAs (one cluster) per pair tile; the cluster shape is compiled in.
+  dim3 grid(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
   if (d.head_dim == 256) {
     PCP_TRY(set_smem_attr<256>());
-    pcp::attn_fwd_kernel<256><<<grid, 192, pcp::AttnSmem<256>::kAlloc, st>>>(tq, tk, tv, to, p);
+    pcp::attn_fwd_pair_kernel<256><<<grid, pcp::kThreads, pcp::PairSmem<256>::kAlloc, st>>>(tq, tk, tv, to, p);
   } else {
     PCP_TRY(set_smem_attr<128>());
-    pcp::attn_fwd_kernel<128><<<grid, 192, pcp::AttnSmem<128>::kAlloc, st>>>(tq, tk, tv, to, p);
+    pcp::attn_fwd_pair_kernel<128><<<grid, pcp::kThreads, pcp::PairSmem<128>::kAlloc, st>>>(tq, tk, tv, to, p);
   }
   CUDA_TRY(cudaGetLastError());
   if (lc) {

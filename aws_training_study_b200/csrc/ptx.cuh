@@ -47,7 +47,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -233,11 +233,114 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_m
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// --------------------------------------------- CTA pairs (cta_group::2) ----
+// A cluster of two CTAs on two SMs shares one MMA: the leader (rank 0)
+// issues tcgen05.mma.cta_group::2, A comes from each CTA's own smem/TMEM
+// (its 128 rows), B is split by N between the two CTAs' smem, and each CTA's
+// TMEM receives the accumulator rows of its A rows.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by a shared::cluster address (possibly the
+// peer CTA's).  Default semantics (release at CTA scope): the data handed over
+// is TMEM, ordered by tcgen05.wait::st + tcgen05.fence::before_thread_sync in
+// the arriving thread and tcgen05.fence::after_thread_sync in the waiter; a
+// cluster-scope release costs ~1.5k cycles here and orders nothing more that
+// the consumer needs.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at offset `bar` of every CTA in `cta_mask` when
+// all tcgen05 ops issued so far by this thread are complete.  (Commit
+// multicast; no data moves.)
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// 3-D tiled TMA load into THIS CTA's smem whose completion bytes are counted
+// on `cluster_bar` (an mbarrier in either CTA of the pair, usually the
+// leader's).  Plain load of local-GPU memory; no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap, int32_t x, int32_t y, int32_t z,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
+      : "memory");
+}
+
 // ------------------------------------------------------------- math -------
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes instead of the MUFU (for x <= ~127): Cody-Waite
+// split x = n + f with n = round(x) obtained by adding 1.5 * 2^23 (which
+// leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a degree-3
+// polynomial fitted here by weighted least squares on relative error (max
+// relative error 7.7e-5, below the 3.9e-3 of the bf16 rounding that follows);
+// n is added to the exponent field with an integer add.  Inputs below -125
+// are clamped so the result stays a normal float (<= 2.4e-38).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float j = __fadd_rn(x, 12582912.0f);
+  const float f = __fsub_rn(x, __fsub_rn(j, 12582912.0f));
+  const float p = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
 
 // Two fp32 -> packed bf16x2 (round to nearest even); `lo` lands in bits [0,16).
