@@ -1,0 +1,84 @@
+// Shared definitions of the history-attention kernel (attn_pair.cuh): tile
+// shape, TMEM map, thread roles, error codes and launch parameters.
+//
+// Every (KV head, 256-row Q tile, key split) work unit computes
+// softmax(Q K^T * scale) V over a contiguous range of 128-key tiles of a
+// dense, compacted bf16 K/V buffer, on a cluster of two CTAs (one per SM)
+// that share each tcgen05 MMA (cta_group::2).
+//
+// Replaces the NKI kernel body of the reference (pcp_attention/kernel.py:
+// 84-554).  Stage map, reference -> here:
+//   resident Q load + pre-scale (kernel.py:141-173) -> TMA load of the CTA's
+//       128 bf16 Q rows into 128B-swizzled smem once; scale applied in fp32.
+//   K/V resident load (kernel.py:295-339) -> TMA producer warp streaming each
+//       CTA's half of every K tile ([64 keys, D]) and V tile ([128 keys, D/2])
+//       through a smem ring holding 2.5 tiles.
+//   QK^T into PSUM (kernel.py:383-394) -> tcgen05.mma kind::f16, M=256 over the
+//       pair, N=128 keys, fp32 accumulator S in TMEM (two buffers).
+//   mask + max + fused exp/sum (kernel.py:396-437) -> two softmax warpgroups
+//       per CTA, one thread per row (TMEM lane) and 64 keys per warpgroup;
+//       exp2 with an fp32 running reference max and sums, partly on the MUFU
+//       and partly as a polynomial on the FMA pipe; keys past the valid count
+//       in the final tile are -inf.
+//   P transpose (kernel.py:439-462) -> none: P is written back to TMEM as bf16
+//       (over S) and used as the A operand of the PV MMA.
+//   PV + rescale (kernel.py:464-511) -> tcgen05.mma A=P (TMEM), B=V (smem,
+//       MN-major), O accumulates in TMEM across all tiles; O is rescaled in
+//       TMEM only when the running max grows by more than 2^8 (lazy rescale).
+//   finalise/store (kernel.py:516-553) -> O/l in fp32, bf16 via swizzled smem
+//       + TMA store, or fp32 partial + log2-sum-exp for the split combine.
+//
+// Thread roles (320 threads per CTA, 1 CTA per SM):
+//   warps 0-7 softmax / correction / epilogue in two warpgroups: warpgroup w
+//     owns key columns [64w, 64w+64) of every S tile and head-dim columns
+//     [w*D/2, (w+1)*D/2) of O,
+//   warp 8 TMA producer, warp 9 TMEM allocator and (leader CTA) the single
+//     thread that issues every MMA of the pair.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include "ptx.cuh"
+
+namespace pcp {
+
+constexpr int kTileM = 128;       // query rows per CTA (TMEM lanes)
+constexpr int kTileN = 128;       // keys per tile
+constexpr int kBoxCols = 64;      // bf16 columns per 128B-swizzled TMA box
+constexpr int kBoxBytes = 128 * 128;  // one box of 128 rows x 128 B
+constexpr int kTmemCols = 512;
+constexpr int kTmemS0 = 256;      // S/P buffers at columns 256 and 384; O at 0
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kSoftmaxWarpgroups = 2;
+constexpr int kSoftmaxThreads = 128 * kSoftmaxWarpgroups;
+constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
+constexpr int kProducerWarp = kSoftmaxThreads / 32;
+constexpr int kMmaWarp = kProducerWarp + 1;
+
+enum : int {
+  kErrWaitQ = 101,
+  kErrWaitKvEmpty = 102,
+  kErrWaitKvFull = 103,
+  kErrWaitPFull = 104,
+  kErrWaitSFull = 105,
+  kErrWaitODone = 106,
+  kErrSmemAlign = 107,
+  kErrWaitRed = 108,
+};
+
+struct AttnParams {
+  int rows_per_head;     // R: query rows sharing one KV head (q_heads_per_kv * Qloc)
+  int m_tiles_per_head;  // ceil(R / 128)
+  int num_kv_heads;
+  int num_keys;          // valid keys in the compacted K/V buffer
+  int tiles_per_split;   // key tiles per split
+  int split_base;        // first split index of this launch in the partial buffers
+  int total_rows;        // num_kv_heads * R
+  float scale_log2;      // softmax_scale * log2(e)
+  int write_final;       // 1: bf16 O via TMA; 0: fp32 partial O + lse
+  float* part_o;         // [splits][total_rows][D]
+  float* part_lse;       // [splits][total_rows]
+  int* err;              // device error word
+};
+
+}  // namespace pcp

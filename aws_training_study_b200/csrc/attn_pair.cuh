@@ -1,9 +1,8 @@
 // History-attention forward on CTA pairs (tcgen05 cta_group::2).
 //
-// Same computation, stages and numerics as attn_fwd_kernel (see that file's
-// header for the map to the reference's NKI kernel, pcp_attention/kernel.py:
-// 84-554), but every work unit is a cluster of two CTAs on two SMs that
-// share one 256-row MMA:
+// Stages, numerics and the map to the reference's NKI kernel
+// (pcp_attention/kernel.py:84-554) are in attn_common.cuh.  Every work unit
+// is a cluster of two CTAs on two SMs that share one 256-row MMA:
 //   * CTA r of the pair owns query rows [256 t + 128 r, +128) of one KV head:
 //     its Q rows in its smem, its S/P and O rows in its TMEM.
 //   * QK^T: S[256, 128 keys] = Q K^T with B = K split by keys: CTA r holds
@@ -23,7 +22,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
-#include "attn_fwd.cuh"
+#include "attn_common.cuh"
 #include "ptx.cuh"
 
 namespace pcp {

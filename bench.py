@@ -453,6 +453,10 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
+    # Rank 0's stdout must carry exactly one JSON line: keep NCCL's version
+    # banner (NCCL_DEBUG=VERSION) off stdout; explicit INFO/TRACE are honoured.
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() in ("VERSION", ""):
+        os.environ["NCCL_DEBUG"] = "WARN"
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     wl = dict(WORKLOADS[args.workload])
