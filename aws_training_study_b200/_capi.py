@@ -15,6 +15,8 @@ LIB_PATH = Path(__file__).resolve().with_name("libpcp_attn.so")
 
 PCP_KV_E4M3 = 0
 PCP_KV_BF16 = 1
+PCP_EXCHANGE_DIRECT = 0
+PCP_EXCHANGE_RING = 1
 
 STATUS_NAMES = {
     0: "PCP_OK",
@@ -80,6 +82,7 @@ SIGNATURES = {
     "pcp_forward": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
     "pcp_device_status": (_c.c_int, [_P, _I32]),
+    "pcp_set_exchange": (_c.c_int, [_P, _I32]),
     "pcp_set_profiling": (_c.c_int, [_P, _I32]),
     "pcp_get_stats": (_c.c_int, [_P, _c.POINTER(PcpStats)]),
     "pcp_destroy": (_c.c_int, [_P]),

@@ -343,7 +343,8 @@ struct pcp_handle {
   cudaStream_t comm_stream = nullptr;
   cudaStream_t last_stream = nullptr;
   cudaEvent_t ev_in = nullptr, ev_comm = nullptr;
-  uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]
+  uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]: slot s receives source s
+  int exchange = PCP_EXCHANGE_DIRECT;
   uint8_t* ws = nullptr;
   Workspace w;
   // staging for pcp_forward_host
@@ -437,23 +438,45 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
     CUDA_TRY(cudaEventRecord(h->ev_in, st));
     CUDA_TRY(cudaStreamWaitEvent(h->comm_stream, h->ev_in, 0));
     const int pc = prof_begin(h, 0, h->comm_stream);
-    for (int hop = 1; hop < P; ++hop) {
-      const int ssrc = ((r - hop + 1) % P + P) % P;
-      const int rsrc = ((r - hop) % P + P) % P;
-      const void* sbuf = hop == 1 ? packed_kv : h->ring + static_cast<size_t>(ssrc) * d.max_local_blocks * pay;
-      void* rbuf = h->ring + static_cast<size_t>(rsrc) * d.max_local_blocks * pay;
-      const size_t sbytes = static_cast<size_t>(ceil_div(valid_len[ssrc], d.block_size)) * pay;
-      const size_t rbytes = static_cast<size_t>(ceil_div(valid_len[rsrc], d.block_size)) * pay;
+    auto slot = [&](int src) { return h->ring + static_cast<size_t>(src) * d.max_local_blocks * pay; };
+    auto live = [&](int src) { return static_cast<size_t>(ceil_div(valid_len[src], d.block_size)) * pay; };
+    if (h->exchange == PCP_EXCHANGE_RING) {
+      // Store-and-forward ring (reference.py:68-71 order, kernel.py:276-293):
+      // hop s sends the shard received at hop s-1 (own shard at s = 1) to
+      // rank+1 and receives source (rank - s) % P from rank-1.
+      for (int hop = 1; hop < P; ++hop) {
+        const int ssrc = ((r - hop + 1) % P + P) % P;
+        const int rsrc = ((r - hop) % P + P) % P;
+        const void* sbuf = hop == 1 ? packed_kv : slot(ssrc);
+        ncclResult_t nr = ncclGroupStart();
+        if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
+        if (live(ssrc)) ncclSend(sbuf, live(ssrc), ncclUint8, (r + 1) % P, h->comm, h->comm_stream);
+        if (live(rsrc)) ncclRecv(slot(rsrc), live(rsrc), ncclUint8, (r - 1 + P) % P, h->comm, h->comm_stream);
+        PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
+        sent += static_cast<int64_t>(live(ssrc));
+      }
+    } else {
+      // Direct exchange over NVSwitch: one NCCL group in which this rank
+      // sends its own shard to every peer and receives every peer's shard
+      // straight from its owner -- the same bytes per rank as the ring, with
+      // no forwarding chain, and still no shard returns to its owner.
       ncclResult_t nr = ncclGroupStart();
       if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
-      if (sbytes) ncclSend(sbuf, sbytes, ncclUint8, (r + 1) % P, h->comm, h->comm_stream);
-      if (rbytes) ncclRecv(rbuf, rbytes, ncclUint8, (r - 1 + P) % P, h->comm, h->comm_stream);
+      for (int step = 1; step < P; ++step) {
+        const int to = (r + step) % P;
+        const int from = ((r - step) % P + P) % P;
+        if (live(r)) ncclSend(packed_kv, live(r), ncclUint8, to, h->comm, h->comm_stream);
+        if (live(from)) ncclRecv(slot(from), live(from), ncclUint8, from, h->comm, h->comm_stream);
+        sent += static_cast<int64_t>(live(r));
+      }
       PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
-      sent += static_cast<int64_t>(sbytes);
-      if (valid_len[rsrc] > 0)
-        remote.srcs.push_back({static_cast<const uint8_t*>(rbuf), valid_len[rsrc],
-                               static_cast<int>(remote.key_off + remote.keys)});
-      remote.keys += valid_len[rsrc];
+    }
+    // Remote keys in ring order: source (rank - s) % P for s = 1..P-1.
+    for (int step = 1; step < P; ++step) {
+      const int src = ((r - step) % P + P) % P;
+      if (valid_len[src] > 0)
+        remote.srcs.push_back({slot(src), valid_len[src], static_cast<int>(remote.key_off + remote.keys)});
+      remote.keys += valid_len[src];
     }
     prof_end(h, pc, h->comm_stream);
     CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
@@ -819,6 +842,14 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms) {
   int err = 0;
   CUDA_TRY(cudaMemcpy(&err, h->ws, sizeof(int), cudaMemcpyDeviceToHost));
   if (err) return fail(PCP_ERR_DEVICE_TIMEOUT, "device wait timed out in the attention kernel (code %d)", err);
+  return PCP_OK;
+}
+
+int pcp_set_exchange(pcp_handle_t* h, int32_t mode) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "exchange mode %d unknown", mode);
+  h->exchange = mode;
   return PCP_OK;
 }
 

@@ -111,6 +111,10 @@ class HistoryAttention:
     CUDA device.  With ``pcp_size > 1`` construction is collective: rank 0
     creates the NCCL id and broadcasts it over ``group`` (any backend; gloo is
     enough), then every rank joins the ring communicator.
+
+    ``exchange`` picks how the shards reach every rank: ``"direct"`` (each
+    rank sends its shard to every peer in one NCCL group; the default on
+    NVSwitch) or ``"ring"`` (the reference's store-and-forward ring).
     """
 
     def __init__(
@@ -120,6 +124,7 @@ class HistoryAttention:
         rank: int | None = None,
         device: int | torch.device | None = None,
         group=None,
+        exchange: str = "direct",
     ):
         self.config = config
         self.kv_dtype = kv_dtype
@@ -152,6 +157,12 @@ class HistoryAttention:
         with torch.cuda.device(self.device):
             _capi.check(lib.pcp_create(ctypes.byref(self._dims), self.rank, self.device.index, uid, ctypes.byref(handle)))
         self._handle = handle
+        modes = {"direct": _capi.PCP_EXCHANGE_DIRECT, "ring": _capi.PCP_EXCHANGE_RING}
+        if exchange not in modes:
+            self.close()
+            raise ValueError(f"exchange must be one of {sorted(modes)}, got {exchange!r}")
+        _capi.check(lib.pcp_set_exchange(self._handle, modes[exchange]))
+        self.exchange = exchange
 
     # -- calls -------------------------------------------------------------
     def _check_inputs(self, q: torch.Tensor, packed_kv: torch.Tensor) -> None:

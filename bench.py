@@ -264,7 +264,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
     q, packed = make_local_baseline_inputs(cfg, args.seed, rank, kv_dtype=kv_dtype, outlier_frac=wl["outliers"],
                                            device=dev)
     valid = cfg.source_valid_lens()
-    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank)
+    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank, exchange=args.exchange)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream()
     flops_step = 4.0 * cfg.num_q_heads * cfg.current_len * cfg.actual_history_len * cfg.head_dim
@@ -396,7 +396,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
                 "block_size": cfg.block_size,
                 "interleave_size": cfg.interleave_size,
                 "kv_dtype": wl["kv"],
-                "parallelism": f"pcp{world} (context-parallel KV ring)",
+                "parallelism": f"pcp{world} (context-parallel, KV shards exchanged '{args.exchange}' over NVLink)",
                 "l2": "inputs larger than L2 (per rank: bf16 K/V working set "
                       f"{2 * cfg.num_kv_heads * sum(valid) * cfg.head_dim * 2 / 2**20:.0f} MiB)",
             },
@@ -442,6 +442,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--exchange", choices=("direct", "ring"), default="direct")
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")
     ap.add_argument("--history", type=int, default=None, help="override the workload's history length (profiling)")
     ap.add_argument("--e2e-steps", type=int, default=10)

@@ -186,6 +186,16 @@ int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_
  * (a peer that left).  On a timeout the NCCL communicator is aborted. */
 int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms);
 
+/* How the shards reach every rank (both send only live blocks and never
+ * return a shard to its owner; outputs are identical up to fp rounding):
+ *   PCP_EXCHANGE_DIRECT (default) -- one NCCL group per forward: each rank
+ *     sends its shard to every peer and receives each peer's shard from its
+ *     owner (NVSwitch gives every pair full bandwidth);
+ *   PCP_EXCHANGE_RING -- the reference's store-and-forward ring
+ *     (kernel.py:276-293): P-1 hops to rank+1, schedule of pcp_ring_schedule. */
+enum pcp_exchange { PCP_EXCHANGE_DIRECT = 0, PCP_EXCHANGE_RING = 1 };
+int pcp_set_exchange(pcp_handle_t* h, int32_t mode);
+
 int pcp_set_profiling(pcp_handle_t* h, int32_t enable);
 int pcp_get_stats(const pcp_handle_t* h, pcp_stats_t* out);
 int pcp_destroy(pcp_handle_t* h);

@@ -18,7 +18,7 @@ CASES = {
 }
 
 
-def _ring_body(rank, world, name):
+def _ring_body(rank, world, name, exchange="direct"):
     import sys
     from pathlib import Path
 
@@ -33,7 +33,7 @@ def _ring_body(rank, world, name):
     torch.cuda.set_device(rank)
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=11, kv_dtype=kv_dtype)
     packed = packed_shards(cfg, k_shards, v_shards)
-    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=rank)
+    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=rank, exchange=exchange)
     qd, kvd = q_shards[rank].cuda(), packed[rank].cuda()
     for _ in range(3):  # repeated calls reuse the ring buffers
         out = attn(qd, kvd)
@@ -52,8 +52,12 @@ def ring_ragged(rank, world):
     return _ring_body(rank, world, "ragged_d128_bf16")
 
 
+def ring_qwen_storeforward(rank, world):
+    return _ring_body(rank, world, "qwen_d256_fp8", exchange="ring")
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged"])
+@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res
