@@ -438,8 +438,15 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
     CUDA_TRY(cudaEventRecord(h->ev_in, st));
     CUDA_TRY(cudaStreamWaitEvent(h->comm_stream, h->ev_in, 0));
     const int pc = prof_begin(h, 0, h->comm_stream);
-    auto slot = [&](int src) { return h->ring + static_cast<size_t>(src) * d.max_local_blocks * pay; };
     auto live = [&](int src) { return static_cast<size_t>(ceil_div(valid_len[src], d.block_size)) * pay; };
+    // All-gather slots are as long as the longest live shard; the other
+    // modes keep one full shard per slot.
+    size_t slot_stride = static_cast<size_t>(d.max_local_blocks) * pay;
+    if (h->exchange == PCP_EXCHANGE_ALLGATHER) {
+      slot_stride = 0;
+      for (int src = 0; src < P; ++src) slot_stride = std::max(slot_stride, live(src));
+    }
+    auto slot = [&](int src) { return h->ring + static_cast<size_t>(src) * slot_stride; };
     if (h->exchange == PCP_EXCHANGE_RING) {
       // Store-and-forward ring (reference.py:68-71 order, kernel.py:276-293):
       // hop s sends the shard received at hop s-1 (own shard at s = 1) to
@@ -454,6 +461,16 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
         if (live(rsrc)) ncclRecv(slot(rsrc), live(rsrc), ncclUint8, (r - 1 + P) % P, h->comm, h->comm_stream);
         PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
         sent += static_cast<int64_t>(live(ssrc));
+      }
+    } else if (h->exchange == PCP_EXCHANGE_ALLGATHER) {
+      // One all-gather of equal-length slots (the longest live shard; at most
+      // one block longer than any other): lets NCCL use NVLink SHARP
+      // (multicast through the switch) where the system offers it.
+      if (slot_stride) {
+        CUDA_TRY(cudaMemcpyAsync(slot(r), packed_kv, live(r), cudaMemcpyDeviceToDevice, h->comm_stream));
+        PCP_TRY(wait_nccl(h->comm, ncclAllGather(slot(r), h->ring, slot_stride, ncclUint8, h->comm, h->comm_stream),
+                          600000));
+        sent += static_cast<int64_t>(slot_stride) * (P - 1);
       }
     } else {
       // Direct exchange over NVSwitch: one NCCL group in which this rank
@@ -847,7 +864,7 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms) {
 
 int pcp_set_exchange(pcp_handle_t* h, int32_t mode) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
-  if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING)
+  if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING && mode != PCP_EXCHANGE_ALLGATHER)
     return fail(PCP_ERR_INVALID_ARGUMENT, "exchange mode %d unknown", mode);
   h->exchange = mode;
   return PCP_OK;

@@ -157,7 +157,8 @@ class HistoryAttention:
         with torch.cuda.device(self.device):
             _capi.check(lib.pcp_create(ctypes.byref(self._dims), self.rank, self.device.index, uid, ctypes.byref(handle)))
         self._handle = handle
-        modes = {"direct": _capi.PCP_EXCHANGE_DIRECT, "ring": _capi.PCP_EXCHANGE_RING}
+        modes = {"direct": _capi.PCP_EXCHANGE_DIRECT, "ring": _capi.PCP_EXCHANGE_RING,
+                 "allgather": _capi.PCP_EXCHANGE_ALLGATHER}
         if exchange not in modes:
             self.close()
             raise ValueError(f"exchange must be one of {sorted(modes)}, got {exchange!r}")

@@ -212,8 +212,10 @@ def run_reference(args, wl, rank: int, world: int) -> int:
     vals, secs = [], []
     flops_total, time_total = 0.0, 0.0
     desc = ""
+    # Each step is a bounded sample; keep the whole run near two minutes.
+    step_s = max(0.5, min(args.ref_step_seconds, 120.0 / max(args.steps, 1)))
     for _ in range(args.steps):
-        tf, dt, rows, desc = cpu_oracle_sample(wl, args.ref_step_seconds)
+        tf, dt, rows, desc = cpu_oracle_sample(wl, step_s)
         vals.append(tf)
         secs.append(dt)
         flops_total += tf * 1e12 * dt
@@ -442,7 +444,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--exchange", choices=("direct", "ring"), default="direct")
+    ap.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")
     ap.add_argument("--history", type=int, default=None, help="override the workload's history length (profiling)")
     ap.add_argument("--e2e-steps", type=int, default=10)

@@ -192,8 +192,10 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms);
  *     sends its shard to every peer and receives each peer's shard from its
  *     owner (NVSwitch gives every pair full bandwidth);
  *   PCP_EXCHANGE_RING -- the reference's store-and-forward ring
- *     (kernel.py:276-293): P-1 hops to rank+1, schedule of pcp_ring_schedule. */
-enum pcp_exchange { PCP_EXCHANGE_DIRECT = 0, PCP_EXCHANGE_RING = 1 };
+ *     (kernel.py:276-293): P-1 hops to rank+1, schedule of pcp_ring_schedule;
+ *   PCP_EXCHANGE_ALLGATHER -- one NCCL all-gather of equal slots sized to the
+ *     longest live shard (lets NCCL multicast through the switch). */
+enum pcp_exchange { PCP_EXCHANGE_DIRECT = 0, PCP_EXCHANGE_RING = 1, PCP_EXCHANGE_ALLGATHER = 2 };
 int pcp_set_exchange(pcp_handle_t* h, int32_t mode);
 
 int pcp_set_profiling(pcp_handle_t* h, int32_t enable);

@@ -56,8 +56,12 @@ def ring_qwen_storeforward(rank, world):
     return _ring_body(rank, world, "qwen_d256_fp8", exchange="ring")
 
 
+def ring_ragged_allgather(rank, world):
+    return _ring_body(rank, world, "ragged_d128_bf16", exchange="allgather")
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward"])
+@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res
