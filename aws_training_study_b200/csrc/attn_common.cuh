@@ -17,9 +17,8 @@
 //       pair, N=128 keys, fp32 accumulator S in TMEM (two buffers).
 //   mask + max + fused exp/sum (kernel.py:396-437) -> two softmax warpgroups
 //       per CTA, one thread per row (TMEM lane) and 64 keys per warpgroup;
-//       exp2 with an fp32 running reference max and sums, partly on the MUFU
-//       and partly as a polynomial on the FMA pipe; keys past the valid count
-//       in the final tile are -inf.
+//       exp2 (MUFU) with an fp32 running reference max and sums; keys past
+//       the valid count in the final tile are -inf.
 //   P transpose (kernel.py:439-462) -> none: P is written back to TMEM as bf16
 //       (over S) and used as the A operand of the PV MMA.
 //   PV + rescale (kernel.py:464-511) -> tcgen05.mma A=P (TMEM), B=V (smem,

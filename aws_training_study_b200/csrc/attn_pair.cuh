@@ -243,11 +243,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = n > 0;
-    // P_j = 2^((s - m_ref) * scale * log2 e) for this warpgroup's 64 keys:
-    // three of every four pairs on the MUFU (ex2.approx), one on the FMA pipe
-    // (exp2_poly), so the 16K exponentials of a tile are not all serialised
-    // on the 16-lane/clk MUFU.  Stores P (bf16) over the S columns and
-    // returns the fp32 sum.
+    // P_j = 2^((s - m_ref) * scale * log2 e) for this warpgroup's 64 keys
+    // (ex2.approx on the MUFU; moving a share of them to an FMA-pipe
+    // polynomial measured slower at both head dims).  Stores P (bf16) over
+    // this warpgroup's S columns and returns the fp32 sum.
     auto make_p = [&](const float* sv, float m, uint32_t t_s) {
       const float neg = -m * sl2;
       float sum0 = 0.f, sum1 = 0.f;
@@ -258,8 +257,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) {
           const float x0 = fmaf(sv[c2 * 32 + 2 * i], sl2, neg);
           const float x1 = fmaf(sv[c2 * 32 + 2 * i + 1], sl2, neg);
-          const float p0 = (i & 3) == 3 ? exp2_poly(x0) : ex2_approx(x0);
-          const float p1 = (i & 3) == 3 ? exp2_poly(x1) : ex2_approx(x1);
+          const float p0 = ex2_approx(x0);
+          const float p1 = ex2_approx(x1);
           sum0 += p0;
           sum1 += p1;
           pk[i] = pack_bf16x2(p0, p1);

@@ -328,21 +328,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes instead of the MUFU (for x <= ~127): Cody-Waite
-// split x = n + f with n = round(x) obtained by adding 1.5 * 2^23 (which
-// leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a degree-3
-// polynomial fitted here by weighted least squares on relative error (max
-// relative error 7.7e-5, below the 3.9e-3 of the bf16 rounding that follows);
-// n is added to the exponent field with an integer add.  Inputs below -125
-// are clamped so the result stays a normal float (<= 2.4e-38).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float j = __fadd_rn(x, 12582912.0f);
-  const float f = __fsub_rn(x, __fsub_rn(j, 12582912.0f));
-  const float p = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
-}
-
 // Two fp32 -> packed bf16x2 (round to nearest even); `lo` lands in bits [0,16).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

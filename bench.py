@@ -65,7 +65,7 @@ def load_peaks() -> dict:
 
 def load_profile_traffic(workload: str, n: int):
     """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / f"attn_fwd_{workload}_p{n}_traffic.txt"
+    p = ROOT / "profiles" / f"attn_pair_{workload}_p{n}_traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
