@@ -343,6 +343,7 @@ struct pcp_handle {
   cudaStream_t comm_stream = nullptr;
   cudaStream_t last_stream = nullptr;
   cudaEvent_t ev_in = nullptr, ev_comm = nullptr;
+  cudaEvent_t ev_group[2] = {nullptr, nullptr};  // direct exchange: shards of each peer group landed
   uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]: slot s receives source s
   int exchange = PCP_EXCHANGE_DIRECT;
   uint8_t* ws = nullptr;
@@ -428,11 +429,15 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
   const int64_t pay = payload_bytes(d);
   const int max_splits = h->w.max_splits;
 
-  Part local, remote;
-  local.key_off = 0;
-  local.keys = valid_len[r];
-  if (valid_len[r] > 0) local.srcs.push_back({static_cast<const uint8_t*>(packed_kv), valid_len[r], 0});
-  remote.key_off = local.keys;
+  // Parts: the local shard, then the remote shards (one part, or one per
+  // peer group with the direct exchange), each attended in its own launch
+  // once its shards have landed; their split partials meet in one combine.
+  std::vector<Part> parts(1);
+  std::vector<cudaEvent_t> ready(1, nullptr);  // event a part waits for (null: none)
+  parts[0].key_off = 0;
+  parts[0].keys = valid_len[r];
+  if (valid_len[r] > 0) parts[0].srcs.push_back({static_cast<const uint8_t*>(packed_kv), valid_len[r], 0});
+  int64_t next_key = parts[0].keys;
   int64_t sent = 0;
   if (P > 1) {
     CUDA_TRY(cudaEventRecord(h->ev_in, st));
@@ -447,6 +452,20 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
       for (int src = 0; src < P; ++src) slot_stride = std::max(slot_stride, live(src));
     }
     auto slot = [&](int src) { return h->ring + static_cast<size_t>(src) * slot_stride; };
+    // Remote part over ring steps [s0, s1): sources (rank - s) % P, in ring order.
+    auto add_part = [&](int s0, int s1, cudaEvent_t ev) {
+      Part part;
+      part.key_off = next_key;
+      for (int step = s0; step < s1; ++step) {
+        const int src = ((r - step) % P + P) % P;
+        if (valid_len[src] > 0)
+          part.srcs.push_back({slot(src), valid_len[src], static_cast<int>(part.key_off + part.keys)});
+        part.keys += valid_len[src];
+      }
+      next_key += part.keys;
+      parts.push_back(part);
+      ready.push_back(ev);
+    };
     if (h->exchange == PCP_EXCHANGE_RING) {
       // Store-and-forward ring (reference.py:68-71 order, kernel.py:276-293):
       // hop s sends the shard received at hop s-1 (own shard at s = 1) to
@@ -462,6 +481,8 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
         PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
         sent += static_cast<int64_t>(live(ssrc));
       }
+      CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
+      add_part(1, P, h->ev_comm);
     } else if (h->exchange == PCP_EXCHANGE_ALLGATHER) {
       // One all-gather of equal-length slots (the longest live shard; at most
       // one block longer than any other): lets NCCL use NVLink SHARP
@@ -472,65 +493,76 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
                           600000));
         sent += static_cast<int64_t>(slot_stride) * (P - 1);
       }
+      CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
+      add_part(1, P, h->ev_comm);
     } else {
-      // Direct exchange over NVSwitch: one NCCL group in which this rank
-      // sends its own shard to every peer and receives every peer's shard
-      // straight from its owner -- the same bytes per rank as the ring, with
-      // no forwarding chain, and still no shard returns to its owner.
-      ncclResult_t nr = ncclGroupStart();
-      if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
-      for (int step = 1; step < P; ++step) {
-        const int to = (r + step) % P;
-        const int from = ((r - step) % P + P) % P;
-        if (live(r)) ncclSend(packed_kv, live(r), ncclUint8, to, h->comm, h->comm_stream);
-        if (live(from)) ncclRecv(slot(from), live(from), ncclUint8, from, h->comm, h->comm_stream);
-        sent += static_cast<int64_t>(live(r));
+      // Direct exchange over NVSwitch: each rank sends its own shard to every
+      // peer and receives every peer's shard straight from its owner -- the
+      // same bytes per rank as the ring, no forwarding chain, and no shard
+      // returns to its owner.  When the local-shard launch fills every SM
+      // pair (so NCCL's kernels only get SMs as it drains) and there are at
+      // least 4 ranks, the peers are exchanged in two NCCL groups (ring steps
+      // 1..ceil((P-1)/2), then the rest) and the first group's shards are
+      // attended while the second group's travel; otherwise one group (fewer
+      // launches and split partials).  Pairs match across ranks: at step s
+      // rank r sends to r+s, which receives from (r+s)-s = r in the same group.
+      Part probe = parts[0];
+      plan_part(d, &probe, h->sms, max_splits);
+      const bool local_fills_gpu =
+          probe.keys && m_units(d) * probe.plan.splits >= std::max(1, h->sms / 2);
+      const int groups = (P >= 4 && local_fills_gpu) ? 2 : 1;
+      const int split_step = 1 + (P - 1 + 1) / 2;
+      for (int g = 0; g < groups; ++g) {
+        const int s0 = g == 0 ? 1 : split_step;
+        const int s1 = (g == 0 && groups == 2) ? split_step : P;
+        ncclResult_t nr = ncclGroupStart();
+        if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
+        for (int step = s0; step < s1; ++step) {
+          const int to = (r + step) % P;
+          const int from = ((r - step) % P + P) % P;
+          if (live(r)) ncclSend(packed_kv, live(r), ncclUint8, to, h->comm, h->comm_stream);
+          if (live(from)) ncclRecv(slot(from), live(from), ncclUint8, from, h->comm, h->comm_stream);
+          sent += static_cast<int64_t>(live(r));
+        }
+        PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
+        CUDA_TRY(cudaEventRecord(h->ev_group[g], h->comm_stream));
+        add_part(s0, s1, h->ev_group[g]);
       }
-      PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
-    }
-    // Remote keys in ring order: source (rank - s) % P for s = 1..P-1.
-    for (int step = 1; step < P; ++step) {
-      const int src = ((r - step) % P + P) % P;
-      if (valid_len[src] > 0)
-        remote.srcs.push_back({slot(src), valid_len[src], static_cast<int>(remote.key_off + remote.keys)});
-      remote.keys += valid_len[src];
     }
     prof_end(h, pc, h->comm_stream);
-    CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
   }
-  plan_part(d, &local, h->sms, max_splits);
-  plan_part(d, &remote, h->sms, max_splits);
-  int splits_local = local.keys ? local.plan.splits : 0;
-  int splits_remote = remote.keys ? remote.plan.splits : 0;
-  if (splits_local + splits_remote > max_splits) {
-    // Keep the total within the partial buffers: shrink the larger part.
-    Part& big = splits_local >= splits_remote ? local : remote;
-    const int other = (&big == &local) ? splits_remote : splits_local;
-    big.plan = plan_splits(m_units(d), ceil_div(big.keys, pcp::kTileN), h->sms, std::max(1, max_splits - other));
-    splits_local = local.keys ? local.plan.splits : 0;
-    splits_remote = remote.keys ? remote.plan.splits : 0;
+  // Split plans; keep the total within the partial buffers by shrinking the
+  // part with the most splits.
+  int total_splits = 0;
+  for (auto& part : parts) {
+    plan_part(d, &part, h->sms, max_splits);
+    total_splits += part.keys ? part.plan.splits : 0;
   }
-  const int total_splits = splits_local + splits_remote;
+  while (total_splits > max_splits) {
+    Part* big = nullptr;
+    for (auto& part : parts)
+      if (part.keys && (!big || part.plan.splits > big->plan.splits)) big = &part;
+    if (!big || big->plan.splits == 1) return fail(PCP_ERR_UNSUPPORTED, "too many launches for the partial buffers");
+    const int others = total_splits - big->plan.splits;
+    big->plan = plan_splits(m_units(d), ceil_div(big->keys, pcp::kTileN), h->sms,
+                            std::max(1, std::min(big->plan.splits - 1, max_splits - others)));
+    total_splits = others + big->plan.splits;
+  }
   const bool direct = total_splits == 1;
   CUDA_TRY(cudaMemsetAsync(h->ws, 0, 4, st));
-
-  if (local.keys) {
+  int split_base = 0;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    if (ready[i]) CUDA_TRY(cudaStreamWaitEvent(st, ready[i], 0));
+    const Part& part = parts[i];
+    if (!part.keys) continue;
     int sp = prof_begin(h, 1, st);
-    PCP_TRY(launch_unpack(d, local.srcs, h->w, h->ws, st, &lc));
+    PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc));
     prof_end(h, sp, st);
     sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, local.key_off, local.keys, local.plan, 0, direct, out, st, &lc));
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, direct, out, st,
+                             &lc));
     prof_end(h, sp, st);
-  }
-  if (P > 1) CUDA_TRY(cudaStreamWaitEvent(st, h->ev_comm, 0));
-  if (remote.keys) {
-    int sp = prof_begin(h, 1, st);
-    PCP_TRY(launch_unpack(d, remote.srcs, h->w, h->ws, st, &lc));
-    prof_end(h, sp, st);
-    sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, remote.key_off, remote.keys, remote.plan, splits_local, direct, out,
-                             st, &lc));
-    prof_end(h, sp, st);
+    split_base += part.plan.splits;
   }
   if (!direct) {
     const int sp = prof_begin(h, 3, st);
@@ -776,7 +808,9 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
     if (cudaStreamCreateWithPriority(&h->comm_stream, cudaStreamNonBlocking, hi) != cudaSuccess)
       return cleanup(fail(PCP_ERR_CUDA, "stream creation failed"));
     if (cudaEventCreateWithFlags(&h->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&h->ev_comm, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&h->ev_comm, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h->ev_group[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h->ev_group[1], cudaEventDisableTiming) != cudaSuccess)
       return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
@@ -927,6 +961,8 @@ int pcp_destroy(pcp_handle_t* h) {
     if (e) cudaEventDestroy(e);
   if (h->ev_in) cudaEventDestroy(h->ev_in);
   if (h->ev_comm) cudaEventDestroy(h->ev_comm);
+  for (auto& e : h->ev_group)
+    if (e) cudaEventDestroy(e);
   if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
   cudaFree(h->ring);
   cudaFree(h->ws);
