@@ -36,6 +36,8 @@ CASES = [
     ("qwen_small_d256", PCPAttentionConfig(8, 1024, 8192, 8192, 512, 64, 32, 2, 256), torch.float8_e4m3fn, [0, 5]),
     ("masked_bf16_d256", PCPAttentionConfig(8, 2048, 32768, 30001, 512, 64, 32, 2, 256), torch.bfloat16, [0, 4, 7]),
     ("gqa8_d128_ragged", PCPAttentionConfig(4, 1024, 8192, 5000, 512, 64, 16, 4, 128), torch.float8_e4m3fn, [0, 2]),
+    # multi-head (no GQA), the official-ring benchmark's shape at small size
+    ("mha_d128_bf16", PCPAttentionConfig(2, 1024, 2048, 2048, 512, 64, 8, 8, 128), torch.bfloat16, [0, 1]),
 ]
 
 
