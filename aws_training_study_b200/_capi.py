@@ -79,8 +79,15 @@ SIGNATURES = {
     "pcp_history_attention_status": (_c.c_int, [_P, _P]),
     "pcp_selftest_bounded_wait": (_c.c_int, [_I32, _PI32]),
     "pcp_history_attention_noalloc": (_c.c_int, [_PDIMS, _P, _P, _I32, _PI32, _P, _P, _P]),
+    "pcp_cache_write": (_c.c_int, [_PDIMS, _I32, _I32, _c.c_int64, _I32, _P, _P, _P, _I32, _P, _c.c_int64, _P, _P]),
+    "pcp_history_attention_paged": (
+        _c.c_int, [_PDIMS, _P, _P, _c.c_int64, _P, _I32, _PI32, _P, _P, _c.c_size_t, _P]),
+    "pcp_prefill_attention_workspace_size": (_c.c_int, [_PDIMS, _c.c_int64, _c.POINTER(_c.c_size_t)]),
+    "pcp_prefill_attention": (_c.c_int, [_PDIMS, _I32, _I32, _P, _P, _I32, _PI32, _P, _P, _P, _P, _c.c_size_t, _P]),
     "pcp_create": (_c.c_int, [_PDIMS, _I32, _I32, _P, _c.POINTER(_P)]),
     "pcp_forward": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_forward_paged": (_c.c_int, [_P, _P, _P, _c.c_int64, _P, _PI32, _P, _P]),
+    "pcp_forward_prefill": (_c.c_int, [_P, _I32, _P, _P, _PI32, _P, _P, _P, _P]),
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
     "pcp_device_status": (_c.c_int, [_P, _I32]),
     "pcp_set_exchange": (_c.c_int, [_P, _I32]),

@@ -63,6 +63,7 @@ enum : int {
   kErrWaitODone = 106,
   kErrSmemAlign = 107,
   kErrWaitRed = 108,
+  kErrBlockTable = 109,  // a block-table entry outside the pool (nothing written or read there)
 };
 
 struct AttnParams {
@@ -78,6 +79,23 @@ struct AttnParams {
   float* part_o;         // [splits][total_rows][D]
   float* part_lse;       // [splits][total_rows]
   int* err;              // device error word
+  // Causal current-token mode (causal != 0): the keys are the current
+  // (prefill) tokens of every rank in global order, key index = global
+  // position.  Query row i of this rank's striped shard sits at global
+  // position (i / I) * (P * I) + rank * I + i % I and sees keys <= it; each
+  // pair tile stops after the key tile holding its last query's position.
+  // Launched with one split.
+  int causal;
+  int q_local_len;       // Qloc
+  int stripe_ranks;      // P
+  int stripe_width;      // I
+  int stripe_rank;       // rank of the query shard
 };
+
+// Global position of local query/key index i of `rank`'s striped shard
+// (pcp_attention/layout.py:19-31).
+__host__ __device__ __forceinline__ int striped_position(int i, int ranks, int width, int rank) {
+  return (i / width) * (ranks * width) + rank * width + i % width;
+}
 
 }  // namespace pcp

@@ -91,7 +91,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pt = pair % p.m_tiles_per_head;
   const int row0 = pt * kPairRows + static_cast<int>(rank) * kTileM;  // first query row of this CTA
   const int split = blockIdx.y;
-  const int n_key_tiles = (p.num_keys + kTileN - 1) / kTileN;
+  int n_key_tiles = (p.num_keys + kTileN - 1) / kTileN;
+  if (p.causal) {
+    // Last key tile any of the pair's 256 rows can see (rows past the end
+    // are padding; a tile that wraps into the next Q head holds Qloc - 1).
+    const int r_first = pt * kPairRows;
+    const int r_last = min(r_first + kPairRows, p.rows_per_head) - 1;
+    const int i_max = (r_first / p.q_local_len != r_last / p.q_local_len) ? p.q_local_len - 1 : r_last % p.q_local_len;
+    const int g_max = striped_position(i_max, p.stripe_ranks, p.stripe_width, p.stripe_rank);
+    n_key_tiles = min(n_key_tiles, g_max / kTileN + 1);
+  }
   const int kt0 = split * p.tiles_per_split;
   const int kt1 = min(kt0 + p.tiles_per_split, n_key_tiles);
   const int n = kt1 - kt0;  // >= 1 by construction on the host
@@ -240,6 +249,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x & (kTileM - 1);  // == TMEM lane
     const uint32_t t_row = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sl2 = p.scale_log2;
+    // Keys this row may see: all valid keys, or (causal) those up to its own
+    // global position -- at least key 0, so the first tile is never empty.
+    int key_limit = p.num_keys;
+    if (p.causal)
+      key_limit = min(key_limit, striped_position((row0 + row) % p.q_local_len, p.stripe_ranks, p.stripe_width,
+                                                  p.stripe_rank) + 1);
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = n > 0;
@@ -281,7 +296,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tmem_ld32(t_s + wg * kHalfKeys, s);
       tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
       tmem_wait_ld();
-      const int valid = p.num_keys - (kt0 + j) * kTileN - wg * kHalfKeys;
+      const int valid = key_limit - (kt0 + j) * kTileN - wg * kHalfKeys;
       if (valid < kHalfKeys) {
 #pragma unroll
         for (int i = 0; i < kHalfKeys; ++i)

@@ -134,6 +134,13 @@ int check_dims(const pcp_dims_t* d) {
   return PCP_OK;
 }
 
+pcp::UnpackSource contiguous_src(const void* base, int valid, int64_t dst_offset) {
+  return {static_cast<const uint8_t*>(base), nullptr, 0, valid, static_cast<int>(dst_offset)};
+}
+pcp::UnpackSource paged_src(const void* pool, const int32_t* table, int64_t pool_blocks, int valid, int64_t dst_offset) {
+  return {static_cast<const uint8_t*>(pool), table, pool_blocks, valid, static_cast<int>(dst_offset)};
+}
+
 int64_t payload_bytes(const pcp_dims_t& d) {
   return 2LL * d.num_kv_heads * d.block_size * d.head_dim * (d.kv_dtype == PCP_KV_BF16 ? 2 : 1);
 }
@@ -218,6 +225,7 @@ int launch_unpack(const pcp_dims_t& d, const std::vector<pcp::UnpackSource>& src
   p.key_stride = static_cast<int>(w.key_stride);
   p.k_out = reinterpret_cast<__nv_bfloat16*>(ws + w.k_off);
   p.v_out = reinterpret_cast<__nv_bfloat16*>(ws + w.v_off);
+  p.err = reinterpret_cast<int*>(ws);
   const int64_t live_blocks = ceil_div(max_valid, d.block_size);
   const int64_t items = live_blocks * 2 * d.num_kv_heads * d.block_size * (d.head_dim / 16);
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 4 * 148));
@@ -228,11 +236,18 @@ int launch_unpack(const pcp_dims_t& d, const std::vector<pcp::UnpackSource>& src
   return PCP_OK;
 }
 
+// Causal current-token launch: the query shard's rank and stripe width
+// (stripe_width 0: plain history launch).
+struct Causal {
+  int rank = 0;
+  int stripe_width = 0;
+};
+
 // Attention over `num_keys` dense keys starting at key `key_off` of the
 // workspace K/V.  Writes bf16 `out` directly (final) or split partials.
 int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uint8_t* ws, int64_t key_off,
                      int64_t num_keys, const SplitPlan& plan, int split_base, bool final_out, void* out,
-                     cudaStream_t st, LaunchCounter* lc) {
+                     cudaStream_t st, LaunchCounter* lc, const Causal& causal = Causal{}) {
   const int64_t R = rows_per_head(d);
   const int64_t mt = ceil_div(R, pcp::kPairRows);  // CTA-pair tiles per KV head
   CUtensorMap tq, tk, tv, to;
@@ -255,6 +270,11 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   p.part_o = reinterpret_cast<float*>(ws + w.po_off);
   p.part_lse = reinterpret_cast<float*>(ws + w.pl_off);
   p.err = reinterpret_cast<int*>(ws);
+  p.causal = causal.stripe_width > 0 ? 1 : 0;
+  p.q_local_len = d.local_q_len;
+  p.stripe_ranks = d.pcp_size;
+  p.stripe_width = std::max(1, causal.stripe_width);
+  p.stripe_rank = causal.rank;
   // Two CTAs (one cluster) per pair tile; the cluster shape is compiled in.
   dim3 grid(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
   if (d.head_dim == 256) {
@@ -270,6 +290,53 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
     lc->attn++;
   }
   return PCP_OK;
+}
+
+// Current tokens of all P ranks ([P][Hkv][Qloc][D] bf16 each for K and V)
+// -> dense workspace keys [key_off, key_off + P * Qloc) in global order.
+int launch_scatter(const pcp_dims_t& d, const void* k_all, const void* v_all, int stripe_width, const Workspace& w,
+                   uint8_t* ws, int64_t key_off, cudaStream_t st, LaunchCounter* lc) {
+  if (reinterpret_cast<uintptr_t>(k_all) % 16 || reinterpret_cast<uintptr_t>(v_all) % 16)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "current K/V must be 16-byte aligned");
+  pcp::ScatterParams p{};
+  p.k_src = static_cast<const __nv_bfloat16*>(k_all);
+  p.v_src = static_cast<const __nv_bfloat16*>(v_all);
+  p.num_sources = d.pcp_size;
+  p.num_kv_heads = d.num_kv_heads;
+  p.local_len = d.local_q_len;
+  p.head_dim = d.head_dim;
+  p.stripe_width = stripe_width;
+  p.key_stride = static_cast<int>(w.key_stride);
+  p.key_off = static_cast<int>(key_off);
+  p.k_out = reinterpret_cast<__nv_bfloat16*>(ws + w.k_off);
+  p.v_out = reinterpret_cast<__nv_bfloat16*>(ws + w.v_off);
+  const int64_t items = 2LL * d.pcp_size * d.num_kv_heads * d.local_q_len * (d.head_dim / 8);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 8 * 148));
+  pcp::current_scatter_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  CUDA_TRY(cudaGetLastError());
+  if (lc) lc->kernels++;
+  return PCP_OK;
+}
+
+// Current-token keys of one forward (global order) and the check of their
+// shape: P * Qloc keys, Qloc a whole number of stripes.
+int64_t current_keys(const pcp_dims_t& d) { return static_cast<int64_t>(d.pcp_size) * d.local_q_len; }
+
+int check_stripe(const pcp_dims_t& d, int stripe_width) {
+  if (stripe_width <= 0 || d.local_q_len % stripe_width)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "interleave_size %d must be positive and divide local_q_len %d",
+                stripe_width, d.local_q_len);
+  if (current_keys(d) > (int64_t(1) << 30)) return fail(PCP_ERR_UNSUPPORTED, "too many current tokens");
+  return PCP_OK;
+}
+
+// The causal current-token launch: one split, every pair tile stops at its
+// last query's position.
+SplitPlan causal_plan(const pcp_dims_t& d) {
+  SplitPlan pl;
+  pl.splits = 1;
+  pl.tiles_per_split = static_cast<int>(ceil_div(current_keys(d), pcp::kTileN));
+  return pl;
 }
 
 int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int splits, void* out, cudaStream_t st,
@@ -344,7 +411,11 @@ struct pcp_handle {
   cudaStream_t last_stream = nullptr;
   cudaEvent_t ev_in = nullptr, ev_comm = nullptr;
   cudaEvent_t ev_group[2] = {nullptr, nullptr};  // direct exchange: shards of each peer group landed
+  cudaEvent_t ev_cur = nullptr;                  // current tokens' K/V of every rank landed
   uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]: slot s receives source s
+  uint8_t* stage = nullptr;  // [max_local_blocks][payload]: a paged shard's blocks gathered for sending
+  uint8_t* cur_k = nullptr;  // [P][Hkv][Qloc][D] bf16: current tokens' K of every rank (P > 1)
+  uint8_t* cur_v = nullptr;
   int exchange = PCP_EXCHANGE_DIRECT;
   uint8_t* ws = nullptr;
   Workspace w;
@@ -408,12 +479,47 @@ void prof_end(pcp_handle* h, int idx, cudaStream_t st) {
   if (idx >= 0) cudaEventRecord(h->spans[idx].end, st);
 }
 
-int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
-                 cudaStream_t st) {
+// This rank's history shard: contiguous packed blocks (table NULL), or
+// logical blocks of a block pool read through a device block table.
+struct LocalKV {
+  const void* base = nullptr;
+  const int32_t* table = nullptr;
+  int64_t pool_blocks = 0;
+};
+
+int launch_block_gather(const pcp_dims_t& d, const LocalKV& local, int live_blocks, void* dst, uint8_t* ws,
+                        cudaStream_t st) {
+  if (live_blocks <= 0) return PCP_OK;
+  pcp::BlockGatherParams p{};
+  p.pool = static_cast<const uint8_t*>(local.base);
+  p.table = local.table;
+  p.pool_blocks = local.pool_blocks;
+  p.live_blocks = live_blocks;
+  p.payload = payload_bytes(d);
+  p.out = static_cast<uint8_t*>(dst);
+  p.err = reinterpret_cast<int*>(ws);
+  const int64_t items = p.payload / 16 * live_blocks;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 2 * 148));
+  pcp::block_gather_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  CUDA_TRY(cudaGetLastError());
+  return PCP_OK;
+}
+
+// k_cur / v_cur (optional, both or neither): this rank's current tokens'
+// K/V shard [Hkv][Qloc][D] bf16, striped like Q with `stripe_width`; they are
+// gathered from every rank and attended causally as one more split.
+int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32_t* valid_len, const void* k_cur,
+                 const void* v_cur, int stripe_width, void* out, cudaStream_t st) {
   const pcp_dims_t& d = h->d;
   const int P = d.pcp_size;
   const int r = h->rank;
-  if (!q || !packed_kv || !valid_len || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (!q || !local.base || !valid_len || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (local.table && local.pool_blocks <= 0) return fail(PCP_ERR_INVALID_ARGUMENT, "empty block pool");
+  const bool with_cur = k_cur != nullptr || v_cur != nullptr;
+  if (with_cur) {
+    if (!k_cur || !v_cur) return fail(PCP_ERR_INVALID_ARGUMENT, "current K and V must both be given");
+    PCP_TRY(check_stripe(d, stripe_width));
+  }
   const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
   int64_t total = 0;
   for (int s = 0; s < P; ++s) {
@@ -422,7 +528,9 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
                   static_cast<long long>(cap));
     total += valid_len[s];
   }
-  if (total == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  if (total == 0 && !with_cur) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  if (total + (with_cur ? current_keys(d) : 0) > h->w.key_stride)
+    return fail(PCP_ERR_UNSUPPORTED, "workspace holds %lld keys", static_cast<long long>(h->w.key_stride));
   CUDA_TRY(cudaSetDevice(h->device));
   h->last_stream = st;
   LaunchCounter lc;
@@ -436,13 +544,28 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
   std::vector<cudaEvent_t> ready(1, nullptr);  // event a part waits for (null: none)
   parts[0].key_off = 0;
   parts[0].keys = valid_len[r];
-  if (valid_len[r] > 0) parts[0].srcs.push_back({static_cast<const uint8_t*>(packed_kv), valid_len[r], 0});
+  if (valid_len[r] > 0)
+    parts[0].srcs.push_back(local.table ? paged_src(local.base, local.table, local.pool_blocks, valid_len[r], 0)
+                                        : contiguous_src(local.base, valid_len[r], 0));
   int64_t next_key = parts[0].keys;
   int64_t sent = 0;
+  // Cleared before the ring stream starts: its block gather may report too.
+  CUDA_TRY(cudaMemsetAsync(h->ws, 0, 4, st));
   if (P > 1) {
     CUDA_TRY(cudaEventRecord(h->ev_in, st));
     CUDA_TRY(cudaStreamWaitEvent(h->comm_stream, h->ev_in, 0));
     const int pc = prof_begin(h, 0, h->comm_stream);
+    if (with_cur) {
+      // Current tokens first: small, and attended right after the local shard.
+      const size_t n = static_cast<size_t>(d.num_kv_heads) * d.local_q_len * d.head_dim;
+      ncclResult_t nr = ncclGroupStart();
+      if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
+      ncclAllGather(k_cur, h->cur_k, n, ncclBfloat16, h->comm, h->comm_stream);
+      ncclAllGather(v_cur, h->cur_v, n, ncclBfloat16, h->comm, h->comm_stream);
+      PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
+      CUDA_TRY(cudaEventRecord(h->ev_cur, h->comm_stream));
+      sent += static_cast<int64_t>(2 * n * 2) * (P - 1);
+    }
     auto live = [&](int src) { return static_cast<size_t>(ceil_div(valid_len[src], d.block_size)) * pay; };
     // All-gather slots are as long as the longest live shard; the other
     // modes keep one full shard per slot.
@@ -452,6 +575,16 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
       for (int src = 0; src < P; ++src) slot_stride = std::max(slot_stride, live(src));
     }
     auto slot = [&](int src) { return h->ring + static_cast<size_t>(src) * slot_stride; };
+    // What this rank sends: its packed shard, or (paged) its live blocks
+    // gathered into a contiguous buffer first -- slot r for the all-gather,
+    // the staging buffer otherwise.
+    const void* own = local.base;
+    if (local.table) {
+      void* dst = h->exchange == PCP_EXCHANGE_ALLGATHER ? static_cast<void*>(slot(r)) : h->stage;
+      PCP_TRY(launch_block_gather(d, local, static_cast<int>(ceil_div(valid_len[r], d.block_size)), dst, h->ws,
+                                  h->comm_stream));
+      own = dst;
+    }
     // Remote part over ring steps [s0, s1): sources (rank - s) % P, in ring order.
     auto add_part = [&](int s0, int s1, cudaEvent_t ev) {
       Part part;
@@ -459,7 +592,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
       for (int step = s0; step < s1; ++step) {
         const int src = ((r - step) % P + P) % P;
         if (valid_len[src] > 0)
-          part.srcs.push_back({slot(src), valid_len[src], static_cast<int>(part.key_off + part.keys)});
+          part.srcs.push_back(contiguous_src(slot(src), valid_len[src], part.key_off + part.keys));
         part.keys += valid_len[src];
       }
       next_key += part.keys;
@@ -473,7 +606,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
       for (int hop = 1; hop < P; ++hop) {
         const int ssrc = ((r - hop + 1) % P + P) % P;
         const int rsrc = ((r - hop) % P + P) % P;
-        const void* sbuf = hop == 1 ? packed_kv : slot(ssrc);
+        const void* sbuf = hop == 1 ? own : slot(ssrc);
         ncclResult_t nr = ncclGroupStart();
         if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
         if (live(ssrc)) ncclSend(sbuf, live(ssrc), ncclUint8, (r + 1) % P, h->comm, h->comm_stream);
@@ -488,7 +621,8 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
       // one block longer than any other): lets NCCL use NVLink SHARP
       // (multicast through the switch) where the system offers it.
       if (slot_stride) {
-        CUDA_TRY(cudaMemcpyAsync(slot(r), packed_kv, live(r), cudaMemcpyDeviceToDevice, h->comm_stream));
+        if (own != slot(r))
+          CUDA_TRY(cudaMemcpyAsync(slot(r), own, live(r), cudaMemcpyDeviceToDevice, h->comm_stream));
         PCP_TRY(wait_nccl(h->comm, ncclAllGather(slot(r), h->ring, slot_stride, ncclUint8, h->comm, h->comm_stream),
                           600000));
         sent += static_cast<int64_t>(slot_stride) * (P - 1);
@@ -520,7 +654,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
         for (int step = s0; step < s1; ++step) {
           const int to = (r + step) % P;
           const int from = ((r - step) % P + P) % P;
-          if (live(r)) ncclSend(packed_kv, live(r), ncclUint8, to, h->comm, h->comm_stream);
+          if (live(r)) ncclSend(own, live(r), ncclUint8, to, h->comm, h->comm_stream);
           if (live(from)) ncclRecv(slot(from), live(from), ncclUint8, from, h->comm, h->comm_stream);
           sent += static_cast<int64_t>(live(r));
         }
@@ -532,26 +666,43 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
     prof_end(h, pc, h->comm_stream);
   }
   // Split plans; keep the total within the partial buffers by shrinking the
-  // part with the most splits.
+  // part with the most splits (the current tokens take one split).
+  const int hist_cap = max_splits - (with_cur ? 1 : 0);
   int total_splits = 0;
   for (auto& part : parts) {
-    plan_part(d, &part, h->sms, max_splits);
+    plan_part(d, &part, h->sms, hist_cap);
     total_splits += part.keys ? part.plan.splits : 0;
   }
-  while (total_splits > max_splits) {
+  while (total_splits > hist_cap) {
     Part* big = nullptr;
     for (auto& part : parts)
       if (part.keys && (!big || part.plan.splits > big->plan.splits)) big = &part;
     if (!big || big->plan.splits == 1) return fail(PCP_ERR_UNSUPPORTED, "too many launches for the partial buffers");
     const int others = total_splits - big->plan.splits;
     big->plan = plan_splits(m_units(d), ceil_div(big->keys, pcp::kTileN), h->sms,
-                            std::max(1, std::min(big->plan.splits - 1, max_splits - others)));
+                            std::max(1, std::min(big->plan.splits - 1, hist_cap - others)));
     total_splits = others + big->plan.splits;
   }
+  if (with_cur) ++total_splits;
   const bool direct = total_splits == 1;
-  CUDA_TRY(cudaMemsetAsync(h->ws, 0, 4, st));
   int split_base = 0;
+  // Current tokens: scatter every rank's shard into sequence order after the
+  // history keys, then one causal launch.
+  auto launch_current = [&]() -> int {
+    if (P > 1) CUDA_TRY(cudaStreamWaitEvent(st, h->ev_cur, 0));
+    int sp = prof_begin(h, 1, st);
+    PCP_TRY(launch_scatter(d, P > 1 ? h->cur_k : k_cur, P > 1 ? h->cur_v : v_cur, stripe_width, h->w, h->ws, total,
+                           st, &lc));
+    prof_end(h, sp, st);
+    sp = prof_begin(h, 2, st);
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, total, current_keys(d), causal_plan(d), split_base, direct, out, st,
+                             &lc, Causal{r, stripe_width}));
+    prof_end(h, sp, st);
+    split_base += 1;
+    return PCP_OK;
+  };
   for (size_t i = 0; i < parts.size(); ++i) {
+    if (i == 1 && with_cur) PCP_TRY(launch_current());
     if (ready[i]) CUDA_TRY(cudaStreamWaitEvent(st, ready[i], 0));
     const Part& part = parts[i];
     if (!part.keys) continue;
@@ -564,6 +715,7 @@ int forward_impl(pcp_handle* h, const void* q, const void* packed_kv, const int3
     prof_end(h, sp, st);
     split_base += part.plan.splits;
   }
+  if (parts.size() == 1 && with_cur) PCP_TRY(launch_current());
   if (!direct) {
     const int sp = prof_begin(h, 3, st);
     PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc));
@@ -656,8 +808,8 @@ int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* pac
       return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
                   static_cast<long long>(cap));
     if (valid_len[s] > 0)
-      part.srcs.push_back({static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
-                           valid_len[s], static_cast<int>(part.keys)});
+      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+                                         valid_len[s], part.keys));
     part.keys += valid_len[s];
   }
   if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
@@ -673,6 +825,159 @@ int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* pac
   const bool direct = part.plan.splits == 1;
   PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
   if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  return PCP_OK;
+}
+
+int pcp_prefill_attention_workspace_size(const pcp_dims_t* dims, int64_t total_valid, size_t* bytes) {
+  PCP_TRY(check_dims(dims));
+  if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
+  int splits = 0;
+  if (total_valid > 0)
+    splits = plan_splits(m_units(*dims), ceil_div(total_valid, pcp::kTileN), num_sms(), max_splits_for(*dims) - 1).splits;
+  *bytes = ws_layout(*dims, total_valid + current_keys(*dims), splits + 1).total;
+  return PCP_OK;
+}
+
+int pcp_prefill_attention(const pcp_dims_t* dims, int32_t interleave_size, int32_t rank, const void* q,
+                          const void* packed_kv, int32_t num_sources, const int32_t* valid_len, const void* k_cur_all,
+                          const void* v_cur_all, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  PCP_TRY(check_dims(dims));
+  const pcp_dims_t& d = *dims;
+  if (!q || (!valid_len && num_sources > 0) || !k_cur_all || !v_cur_all || !out || !workspace)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  PCP_TRY(check_stripe(d, interleave_size));
+  if (rank < 0 || rank >= d.pcp_size) return fail(PCP_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, d.pcp_size);
+  if (num_sources < 0 || num_sources > pcp::kMaxSources)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [0, %d]", num_sources, pcp::kMaxSources);
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  const int64_t pay = payload_bytes(d);
+  Part part;
+  for (int s = 0; s < num_sources; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    if (valid_len[s] > 0) {
+      if (!packed_kv) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL packed_kv");
+      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+                                         valid_len[s], part.keys));
+    }
+    part.keys += valid_len[s];
+  }
+  const int sms = num_sms();
+  int splits = 0;
+  if (part.keys) {
+    plan_part(d, &part, sms, max_splits_for(d) - 1);
+    splits = part.plan.splits;
+  }
+  const Workspace w = ws_layout(d, part.keys + current_keys(d), splits + 1);
+  if (workspace_bytes < w.total)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
+  auto* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool direct = splits == 0;
+  CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
+  if (part.keys) {
+    PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+    PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, false, out, st, nullptr));
+  }
+  PCP_TRY(launch_scatter(d, k_cur_all, v_cur_all, interleave_size, w, ws, part.keys, st, nullptr));
+  PCP_TRY(launch_attention(d, q, w, ws, part.keys, current_keys(d), causal_plan(d), splits, direct, out, st, nullptr,
+                           Causal{rank, interleave_size}));
+  if (!direct) PCP_TRY(launch_combine(d, w, ws, splits + 1, out, st, nullptr));
+  return PCP_OK;
+}
+
+int pcp_history_attention_paged(const pcp_dims_t* dims, const void* q, const void* cache_pool, int64_t pool_blocks,
+                                const int32_t* block_tables, int32_t num_sources, const int32_t* valid_len, void* out,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  PCP_TRY(check_dims(dims));
+  const pcp_dims_t& d = *dims;
+  if (!q || !cache_pool || !block_tables || !valid_len || !out || !workspace)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (pool_blocks <= 0) return fail(PCP_ERR_INVALID_ARGUMENT, "empty block pool");
+  if (num_sources <= 0 || num_sources > pcp::kMaxSources)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  Part part;
+  for (int s = 0; s < num_sources; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    if (valid_len[s] > 0)
+      part.srcs.push_back(paged_src(cache_pool, block_tables + static_cast<size_t>(s) * d.max_local_blocks, pool_blocks,
+                                    valid_len[s], part.keys));
+    part.keys += valid_len[s];
+  }
+  if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+  plan_part(d, &part, num_sms(), max_splits_for(d));
+  const Workspace w = ws_layout(d, part.keys, part.plan.splits);
+  if (workspace_bytes < w.total)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
+  auto* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
+  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+  const bool direct = part.plan.splits == 1;
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
+  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  return PCP_OK;
+}
+
+int pcp_cache_write(const pcp_dims_t* dims, int32_t interleave_size, int32_t rank, int64_t first_position,
+                    int32_t num_tokens, const void* k_src, const void* v_src, const int32_t* block_table,
+                    int32_t table_len, void* cache_pool, int64_t pool_blocks, int32_t* device_status, void* stream) {
+  PCP_TRY(check_dims(dims));
+  const pcp_dims_t& d = *dims;
+  if ((num_tokens > 0 && (!k_src || !v_src)) || !block_table || !cache_pool || !device_status)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
+  if (interleave_size <= 0 || d.block_size % interleave_size)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "interleave_size %d must be positive and divide block_size %d",
+                interleave_size, d.block_size);
+  if (rank < 0 || rank >= d.pcp_size) return fail(PCP_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, d.pcp_size);
+  if (first_position < 0 || num_tokens < 0 || table_len < 0 || pool_blocks <= 0)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "negative position / token count / table length or empty pool");
+  if (reinterpret_cast<uintptr_t>(k_src) % 16 || reinterpret_cast<uintptr_t>(v_src) % 16 ||
+      reinterpret_cast<uintptr_t>(cache_pool) % 16)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "K/V sources and the pool must be 16-byte aligned");
+  // Slots this rank owns below position x: whole stripes of P*I, plus the
+  // part of the last one that reaches into this rank's I positions.
+  const int64_t stride = static_cast<int64_t>(d.pcp_size) * interleave_size;
+  auto owned_below = [&](int64_t x) {
+    return (x / stride) * interleave_size +
+           std::min<int64_t>(std::max<int64_t>(x % stride - static_cast<int64_t>(rank) * interleave_size, 0),
+                             interleave_size);
+  };
+  const int64_t local0 = owned_below(first_position);
+  const int64_t owned = owned_below(first_position + num_tokens) - local0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemsetAsync(device_status, 0, sizeof(int32_t), st));
+  if (owned == 0) return PCP_OK;
+  if (ceil_div(local0 + owned, d.block_size) > table_len)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "block table of %d entries is too short for local slot %lld", table_len,
+                static_cast<long long>(local0 + owned - 1));
+  pcp::CacheWriteParams p{};
+  p.k_src = static_cast<const __nv_bfloat16*>(k_src);
+  p.v_src = static_cast<const __nv_bfloat16*>(v_src);
+  p.num_tokens = num_tokens;
+  p.first = first_position;
+  p.local0 = local0;
+  p.owned = static_cast<int>(owned);
+  p.ranks = d.pcp_size;
+  p.width = interleave_size;
+  p.rank = rank;
+  p.num_kv_heads = d.num_kv_heads;
+  p.block_size = d.block_size;
+  p.head_dim = d.head_dim;
+  p.kv_is_bf16 = d.kv_dtype == PCP_KV_BF16;
+  p.table = block_table;
+  p.table_len = table_len;
+  p.pool_blocks = pool_blocks;
+  p.pool = static_cast<uint8_t*>(cache_pool);
+  p.err = device_status;
+  const int64_t items = 2 * owned * d.num_kv_heads * (d.head_dim / 8);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 4 * 148));
+  pcp::cache_write_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  CUDA_TRY(cudaGetLastError());
   return PCP_OK;
 }
 
@@ -739,8 +1044,8 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
       return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
                   static_cast<long long>(cap));
     if (valid_len[s] > 0)
-      part.srcs.push_back({static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
-                           valid_len[s], static_cast<int>(part.keys)});
+      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+                                         valid_len[s], part.keys));
     part.keys += valid_len[s];
   }
   if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
@@ -794,7 +1099,8 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
     pcp_destroy(h);
     return code;
   };
-  const int64_t key_cap = static_cast<int64_t>(d.pcp_size) * d.max_local_blocks * d.block_size;
+  // Dense keys: every source's history plus the current tokens of a prefill.
+  const int64_t key_cap = static_cast<int64_t>(d.pcp_size) * d.max_local_blocks * d.block_size + current_keys(d);
   h->w = ws_layout(d, key_cap, max_splits_for(d));
   if (cudaMalloc(&h->ws, h->w.total) != cudaSuccess)
     return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu workspace bytes failed", h->w.total));
@@ -803,6 +1109,12 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
     const size_t ring_bytes = static_cast<size_t>(d.pcp_size) * d.max_local_blocks * payload_bytes(d);
     if (cudaMalloc(&h->ring, ring_bytes) != cudaSuccess)
       return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu ring bytes failed", ring_bytes));
+    const size_t stage_bytes = static_cast<size_t>(d.max_local_blocks) * payload_bytes(d);
+    if (cudaMalloc(&h->stage, stage_bytes) != cudaSuccess)
+      return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu staging bytes failed", stage_bytes));
+    const size_t cur_bytes = static_cast<size_t>(current_keys(d)) * d.num_kv_heads * d.head_dim * 2;
+    if (cudaMalloc(&h->cur_k, cur_bytes) != cudaSuccess || cudaMalloc(&h->cur_v, cur_bytes) != cudaSuccess)
+      return cleanup(fail(PCP_ERR_OUT_OF_MEMORY, "cudaMalloc of 2 x %zu current-token bytes failed", cur_bytes));
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
     if (cudaStreamCreateWithPriority(&h->comm_stream, cudaStreamNonBlocking, hi) != cudaSuccess)
@@ -810,7 +1122,8 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
     if (cudaEventCreateWithFlags(&h->ev_in, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&h->ev_comm, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&h->ev_group[0], cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&h->ev_group[1], cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&h->ev_group[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&h->ev_cur, cudaEventDisableTiming) != cudaSuccess)
       return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
@@ -831,7 +1144,31 @@ int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int
                 void* stream) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
   if (h->comm_failed) return fail(PCP_ERR_PEER, "the ring communicator was aborted");
-  return forward_impl(h, q, packed_kv, valid_len, out, static_cast<cudaStream_t>(stream));
+  LocalKV local;
+  local.base = packed_kv;
+  return forward_impl(h, q, local, valid_len, nullptr, nullptr, 0, out, static_cast<cudaStream_t>(stream));
+}
+
+int pcp_forward_paged(pcp_handle_t* h, const void* q, const void* cache_pool, int64_t pool_blocks,
+                      const int32_t* block_table, const int32_t* valid_len, void* out, void* stream) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (h->comm_failed) return fail(PCP_ERR_PEER, "the ring communicator was aborted");
+  if (!block_table) return fail(PCP_ERR_INVALID_ARGUMENT, "block_table is NULL");
+  LocalKV local;
+  local.base = cache_pool;
+  local.table = block_table;
+  local.pool_blocks = pool_blocks;
+  return forward_impl(h, q, local, valid_len, nullptr, nullptr, 0, out, static_cast<cudaStream_t>(stream));
+}
+
+int pcp_forward_prefill(pcp_handle_t* h, int32_t interleave_size, const void* q, const void* packed_kv,
+                        const int32_t* valid_len, const void* k_cur, const void* v_cur, void* out, void* stream) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (h->comm_failed) return fail(PCP_ERR_PEER, "the ring communicator was aborted");
+  if (!k_cur || !v_cur) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL current K/V");
+  LocalKV local;
+  local.base = packed_kv;
+  return forward_impl(h, q, local, valid_len, k_cur, v_cur, interleave_size, out, static_cast<cudaStream_t>(stream));
 }
 
 int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
@@ -963,8 +1300,12 @@ int pcp_destroy(pcp_handle_t* h) {
   if (h->ev_comm) cudaEventDestroy(h->ev_comm);
   for (auto& e : h->ev_group)
     if (e) cudaEventDestroy(e);
+  if (h->ev_cur) cudaEventDestroy(h->ev_cur);
   if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
   cudaFree(h->ring);
+  cudaFree(h->stage);
+  cudaFree(h->cur_k);
+  cudaFree(h->cur_v);
   cudaFree(h->ws);
   cudaFree(h->dq);
   cudaFree(h->dkv);

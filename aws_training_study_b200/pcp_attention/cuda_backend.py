@@ -205,6 +205,60 @@ class HistoryAttention:
             )
         return out
 
+    def forward_paged(self, q: torch.Tensor, pool: torch.Tensor, block_table: torch.Tensor, valid_len=None,
+                      out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """``__call__`` with this rank's history shard in a block pool
+        (``[pool_blocks, payload]``, see ``paged.make_pool``): logical block b
+        is pool block ``block_table[b]`` (int32 ``[max_local_blocks]`` on the
+        device)."""
+        cfg = self.config
+        if tuple(q.shape) != (cfg.num_q_heads, cfg.local_q_len, cfg.head_dim) or q.dtype != torch.bfloat16:
+            raise ValueError("bad Q")
+        if pool.dim() != 2 or pool.shape[1] != payload_elements(cfg) or pool.dtype != self.kv_dtype:
+            raise ValueError(f"pool must be [blocks, {payload_elements(cfg)}] {self.kv_dtype}")
+        if block_table.dtype != torch.int32 or block_table.numel() != cfg.max_local_blocks:
+            raise ValueError(f"block_table must be int32 [{cfg.max_local_blocks}]")
+        for name, t in (("q", q), ("pool", pool), ("block_table", block_table)):
+            if t.device != self.device or not t.is_contiguous():
+                raise ValueError(f"{name} must be contiguous on {self.device}")
+        if out is None:
+            out = torch.empty_like(q)
+        vals = self._valid(valid_len)
+        with torch.cuda.device(self.device):
+            _capi.check(
+                _capi.lib().pcp_forward_paged(
+                    self._handle, ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(pool.data_ptr()),
+                    int(pool.shape[0]), ctypes.c_void_p(block_table.data_ptr()), vals,
+                    ctypes.c_void_p(out.data_ptr()), _cuda_stream_ptr(stream)
+                )
+            )
+        return out
+
+    def prefill(self, q: torch.Tensor, packed_kv: torch.Tensor, k_cur: torch.Tensor, v_cur: torch.Tensor,
+                valid_len=None, out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """History attention plus causal attention over the current (prefill)
+        tokens of every rank, merged by log-sum-exp.  ``k_cur``/``v_cur`` are
+        this rank's current tokens' K/V shard ``[Hkv, Qloc, D]`` bf16, striped
+        like ``q`` (``shard_query`` layout); a query sees every history key and
+        the current keys at global positions up to its own."""
+        self._check_inputs(q, packed_kv)
+        _check_current(self.config, k_cur, v_cur, False, self.device)
+        if out is None:
+            out = torch.empty_like(q)
+        elif tuple(out.shape) != tuple(q.shape) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous bf16 tensor shaped like q")
+        vals = self._valid(valid_len)
+        with torch.cuda.device(self.device):
+            _capi.check(
+                _capi.lib().pcp_forward_prefill(
+                    self._handle, self.config.interleave_size, ctypes.c_void_p(q.data_ptr()),
+                    ctypes.c_void_p(packed_kv.data_ptr()), vals, ctypes.c_void_p(k_cur.data_ptr()),
+                    ctypes.c_void_p(v_cur.data_ptr()), ctypes.c_void_p(out.data_ptr()), _cuda_stream_ptr(stream)
+                )
+            )
+        return out
+
     def forward_host(self, q: torch.Tensor, packed_kv: torch.Tensor, valid_len=None, out: torch.Tensor | None = None,
                      stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """End-to-end call with host tensors: H2D copies, forward, D2H copy, sync."""
@@ -249,6 +303,70 @@ class HistoryAttention:
             self.close()
         except Exception:
             pass
+
+
+def _check_current(config: PCPAttentionConfig, k_cur: torch.Tensor, v_cur: torch.Tensor, all_ranks: bool,
+                   device: torch.device | None) -> None:
+    shape = (config.num_kv_heads, config.local_q_len, config.head_dim)
+    if all_ranks:
+        shape = (config.pcp_size,) + shape
+    for name, t in (("k_cur", k_cur), ("v_cur", v_cur)):
+        if tuple(t.shape) != shape or t.dtype != torch.bfloat16:
+            raise ValueError(f"expected {name} {shape} bf16, got {tuple(t.shape)} {t.dtype}")
+        if not t.is_cuda or not t.is_contiguous() or (device is not None and t.device != device):
+            raise ValueError(f"{name} must be a contiguous CUDA tensor on {device}")
+    if config.local_q_len % config.interleave_size:
+        raise ValueError("interleave_size must divide local_q_len")
+
+
+def prefill_attention_single(q: torch.Tensor, packed_kv: torch.Tensor | None, valid_len, k_cur_all: torch.Tensor,
+                             v_cur_all: torch.Tensor, config: PCPAttentionConfig, rank: int,
+                             kv_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+                             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Stateless single-GPU prefill (``pcp_prefill_attention``): rank
+    ``rank``'s Q shard against ``len(valid_len)`` resident history shards
+    (as in ``history_attention_single``) and, causally, the current tokens of
+    all ``pcp_size`` ranks, ``k_cur_all``/``v_cur_all`` ``[P, Hkv, Qloc, D]``
+    bf16 (rank s's striped shard at index s)."""
+    vals = [int(v) for v in valid_len]
+    nsrc = len(vals)
+    if packed_kv is None:
+        if any(vals):
+            raise ValueError("history tokens given without packed_kv")
+        kv_dtype = kv_dtype or torch.float8_e4m3fn
+    else:
+        kv_dtype = kv_dtype or packed_kv.dtype
+        if tuple(packed_kv.shape) != (nsrc * config.max_local_blocks, payload_elements(config)):
+            raise ValueError(f"packed KV must be [{nsrc * config.max_local_blocks}, {payload_elements(config)}]")
+        if not (packed_kv.is_cuda and packed_kv.is_contiguous()):
+            raise ValueError("packed_kv must be a contiguous CUDA tensor")
+    dims = make_dims(config, kv_dtype)
+    if q.dtype != torch.bfloat16 or tuple(q.shape) != (config.num_q_heads, config.local_q_len, config.head_dim):
+        raise ValueError("bad Q")
+    if not (q.is_cuda and q.is_contiguous()):
+        raise ValueError("q must be a contiguous CUDA tensor")
+    _check_current(config, k_cur_all, v_cur_all, True, q.device)
+    if not 0 <= rank < config.pcp_size:
+        raise ValueError(f"rank {rank} outside [0, {config.pcp_size})")
+    lib = _capi.lib()
+    nbytes = ctypes.c_size_t()
+    _capi.check(lib.pcp_prefill_attention_workspace_size(ctypes.byref(dims), sum(vals), ctypes.byref(nbytes)))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty_like(q)
+    kv_ptr = packed_kv.data_ptr() if packed_kv is not None else 0
+    with torch.cuda.device(q.device):
+        _capi.check(
+            lib.pcp_prefill_attention(
+                ctypes.byref(dims), config.interleave_size, rank, ctypes.c_void_p(q.data_ptr()),
+                ctypes.c_void_p(kv_ptr), nsrc, _capi.int32_array(vals) if nsrc else None,
+                ctypes.c_void_p(k_cur_all.data_ptr()), ctypes.c_void_p(v_cur_all.data_ptr()),
+                ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()), nbytes.value,
+                _cuda_stream_ptr(stream)
+            )
+        )
+        _capi.check(lib.pcp_history_attention_status(ctypes.c_void_p(ws.data_ptr()), _cuda_stream_ptr(stream)))
+    return out
 
 
 def history_attention_single(q: torch.Tensor, packed_kv: torch.Tensor, valid_len, config: PCPAttentionConfig,

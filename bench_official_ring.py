@@ -43,6 +43,8 @@ def parse_args() -> argparse.Namespace:
     parser.add_argument("--iterations", type=int, default=20)
     parser.add_argument("--seed", type=int, default=20260907)
     parser.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
+    parser.add_argument("--phases", action="store_true",
+                        help="after timing, profile a few calls and print rank 0's per-phase device time")
     return parser.parse_args()
 
 
@@ -116,8 +118,19 @@ def main() -> int:
     if world > 1:
         samples = [None] * world
         dist.all_gather_object(samples, (dev_ms, host_ms))
+    phases = None
+    if args.phases:
+        attn.set_profiling(True)
+        for _ in range(5):
+            attn(q_dev, kv_dev, valid)
+        attn.status()
+        st = attn.stats()
+        attn.set_profiling(False)
+        phases = {k: (st[k] / st["forwards"] if k.endswith("_ms") else st[k]) for k in st}
     if rank == 0:
         useful_flops = 4 * H * D * S * S
+        if phases:
+            print(f"official_ring_benchmark[phases rank0]: {phases}", flush=True)
         for label, idx in (("device", 0), ("host", 1)):
             per_iter = [max(r[idx][i] for r in samples) for i in range(args.iterations)]
             mean_ms = statistics.fmean(per_iter)

@@ -127,6 +127,61 @@ int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* pac
  * `workspace` by the last pcp_history_attention on it (PCP_ERR_DEVICE_TIMEOUT). */
 int pcp_history_attention_status(const void* workspace, void* stream);
 
+/* ---- paged KV cache: producer and block-table consumer ------------------ */
+
+/* The paged-cache producer (no device counterpart in the reference, which
+ * builds its caches on the host with shard_history + pack_local_kv,
+ * layout.py:54-98 and kernel.py:17-29, quantising with
+ * tensor.to(torch.float8_e4m3fn) in run_poc.py:81-134).  Writes new tokens'
+ * K and V into THIS rank's paged cache, quantised to dims->kv_dtype:
+ *   - k_src / v_src: [Hkv][num_tokens][D] bf16 in sequence order (device);
+ *     token t sits at absolute history position first_position + t.
+ *   - Position p belongs to rank (p / I) % P at local slot
+ *     (p / (P * I)) * I + p % I; only this rank's tokens are written (every
+ *     rank may pass the same sources).  Slot l lives in logical block l / bs,
+ *     row l % bs, and logical block b is pool block block_table[b]
+ *     (block_table: DEVICE int32[table_len]).
+ *   - cache_pool: [pool_blocks][2 * Hkv * bs * D] in the packed payload
+ *     format (per block all K rows of every head, then all V rows).
+ *   - e4m3fn: round to nearest even; magnitudes above 464 and NaN/Inf become
+ *     NaN (0x7F | sign), as torch's cast does.  bf16 caches are copied.
+ *   - device_status: caller-owned DEVICE int32, zeroed here and set to 109 if
+ *     a table entry lies outside the pool (that token is skipped).
+ *   - interleave_size I must divide block_size. */
+int pcp_cache_write(const pcp_dims_t* dims, int32_t interleave_size, int32_t rank, int64_t first_position,
+                    int32_t num_tokens, const void* k_src, const void* v_src, const int32_t* block_table,
+                    int32_t table_len, void* cache_pool, int64_t pool_blocks, int32_t* device_status, void* stream);
+
+/* pcp_history_attention over paged shards: source s's logical blocks are
+ * pool blocks block_tables[s * max_local_blocks + b] (DEVICE int32) of one
+ * cache_pool [pool_blocks][payload].  A table entry outside the pool is
+ * skipped and reported as code 109 by pcp_history_attention_status.
+ * Workspace: pcp_history_attention_workspace_size. */
+int pcp_history_attention_paged(const pcp_dims_t* dims, const void* q, const void* cache_pool, int64_t pool_blocks,
+                                const int32_t* block_tables, int32_t num_sources, const int32_t* valid_len, void* out,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- prefill: history plus causal current-token attention -------------- */
+
+/* The reference leaves current-token attention for later (README.md:17-18):
+ * its kernel attends the Q shard to the history only.  These entries add the
+ * adjacent step of the same prefill layer: each query also attends, causally,
+ * to the current (prefill) tokens of every rank, and the two parts merge
+ * through the same (O, log-sum-exp) combine as the history splits.
+ *   - Current tokens are striped across ranks exactly like Q (layout.py:34-51,
+ *     global position of local token i of rank s is
+ *     (i / I) * (P * I) + s * I + i % I); a query at global position g sees
+ *     every history key and the current keys at positions <= g.
+ *   - k_cur_all / v_cur_all: the current tokens' K and V of ALL ranks,
+ *     [pcp_size][Hkv][Qloc][D] bf16, rank s's shard at index s.
+ *   - `rank`: which rank's Q shard `q` is.  interleave_size I must divide Qloc.
+ *   - Zero history tokens (valid_len all 0, packed_kv may then be NULL) is a
+ *     plain causal prefill. */
+int pcp_prefill_attention_workspace_size(const pcp_dims_t* dims, int64_t total_valid, size_t* bytes);
+int pcp_prefill_attention(const pcp_dims_t* dims, int32_t interleave_size, int32_t rank, const void* q,
+                          const void* packed_kv, int32_t num_sources, const int32_t* valid_len, const void* k_cur_all,
+                          const void* v_cur_all, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Failure-detection self test: runs one kernel that waits on an mbarrier
  * nothing arrives at, bounded by limit_us of device time, and returns the
  * device error word it recorded (199 when the bound fired) in *device_status.
@@ -176,7 +231,23 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
 int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
                 void* stream);
 
-/* Same, with HOST buffers (pinned or pageable): copies q and packed_kv in,
+/* pcp_forward with this rank's shard in a paged cache: its logical block b is
+ * pool block block_table[b] (DEVICE int32[max_local_blocks]) of cache_pool
+ * [pool_blocks][payload].  The live blocks are gathered into a contiguous
+ * buffer on the ring stream before they are sent; the local part reads the
+ * pool directly. */
+int pcp_forward_paged(pcp_handle_t* h, const void* q, const void* cache_pool, int64_t pool_blocks,
+                      const int32_t* block_table, const int32_t* valid_len, void* out, void* stream);
+
+/* pcp_forward plus causal attention over the current tokens (see
+ * pcp_prefill_attention): k_cur / v_cur are THIS rank's current tokens' K and
+ * V shard, [Hkv][Qloc][D] bf16 on the device, striped like q.  The shards of
+ * all ranks are all-gathered on the ring stream before the history exchange
+ * and attended right after the local history shard. */
+int pcp_forward_prefill(pcp_handle_t* h, int32_t interleave_size, const void* q, const void* packed_kv,
+                        const int32_t* valid_len, const void* k_cur, const void* v_cur, void* out, void* stream);
+
+/* Same as pcp_forward, with HOST buffers (pinned or pageable): copies q and packed_kv in,
  * runs pcp_forward on `stream`, copies out back, and synchronises `stream`. */
 int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
                      void* out_host, void* stream);

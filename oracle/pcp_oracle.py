@@ -356,3 +356,96 @@ def history_flops(num_q_heads: int, q_len: int, hist_len: int, head_dim: int) ->
     """QK^T plus PV model FLOPs, ``4 * Hq * Q * Hist * D`` (reference README
     MFU formula, ``README.md:167-171``)."""
     return 4.0 * num_q_heads * q_len * hist_len * head_dim
+
+
+# ----------------------------------------------------------------------------
+# Prefill: history plus causal current-token attention.
+#
+# The reference stops at history-only attention and lists current-token
+# attention as future work (``README.md:17-18``), so nothing upstream pins
+# this part directly.  It is restated from the definition of causal prefill
+# attention over a cached prefix: a current token at global position g (in
+# the ``shard_query`` stripe layout, ``layout.py:19-51``) attends to every
+# history key and to the current tokens at positions <= g, in one softmax.
+# The history half is exactly ``dense_history_attention`` (pinned above).
+# ----------------------------------------------------------------------------
+
+def prefill_attention(q_shard: np.ndarray, k_hist: np.ndarray, v_hist: np.ndarray, k_cur: np.ndarray,
+                      v_cur: np.ndarray, cfg: OracleConfig, rank: int, row_chunk: int = 1024) -> np.ndarray:
+    """Rank ``rank``'s striped Q shard ``[Hq, Qloc, D]`` against the dense
+    history K/V ``[Hkv, A, D]`` (A may be 0) and the current tokens' K/V in
+    sequence order ``[Hkv, current_len, D]``, causally -> fp32 ``[Hq, Qloc, D]``."""
+    hq, nq, dim = q_shard.shape
+    hkv = k_cur.shape[0]
+    if hq % hkv or k_cur.shape != v_cur.shape or k_hist.shape[0] != hkv or k_cur.shape[1] != cfg.current_len:
+        raise ValueError("incompatible shapes for prefill attention")
+    group = hq // hkv
+    qpos = global_positions_for_rank(cfg.current_len, rank, cfg.pcp_size, cfg.interleave_size)
+    if qpos.shape[0] != nq:
+        raise ValueError("Q shard length does not match the stripe layout")
+    kpos = np.arange(cfg.current_len, dtype=np.int64)
+    kh, vh = k_hist.astype(np.float32, copy=False), v_hist.astype(np.float32, copy=False)
+    kc, vc = k_cur.astype(np.float32, copy=False), v_cur.astype(np.float32, copy=False)
+    scale = np.float32(1.0 / math.sqrt(dim))
+    out = np.empty((hq, nq, dim), dtype=np.float32)
+    for h in range(hq):
+        g = h // group
+        keys = np.concatenate([kh[g], kc[g]], axis=0)
+        vals = np.concatenate([vh[g], vc[g]], axis=0)
+        for r0 in range(0, nq, row_chunk):
+            qs = q_shard[h, r0 : r0 + row_chunk].astype(np.float32)
+            s = (qs @ keys.T) * scale
+            future = kpos[None, :] > qpos[r0 : r0 + row_chunk, None]
+            s[:, kh.shape[1]:][future] = -np.inf
+            s -= s.max(axis=-1, keepdims=True)
+            np.exp(s, out=s)
+            s /= s.sum(axis=-1, keepdims=True)
+            out[h, r0 : r0 + row_chunk] = s @ vals
+    return out
+
+
+def prefill_flops(cfg: OracleConfig, rank: int) -> float:
+    """Useful FLOPs of one rank's prefill: the history part plus the causal
+    pairs (query, visible current key) only."""
+    qpos = global_positions_for_rank(cfg.current_len, rank, cfg.pcp_size, cfg.interleave_size)
+    causal_pairs = float((qpos + 1).sum())
+    return 4.0 * cfg.num_q_heads * (qpos.shape[0] * cfg.actual_history_len + causal_pairs) * cfg.head_dim
+
+
+# ----------------------------------------------------------------------------
+# Paged-cache producer.
+#
+# The reference builds caches on the host (``shard_history``, ``layout.py:
+# 54-98``; ``pack_local_kv``, ``kernel.py:17-29``; e4m3 from ``tensor.to(
+# torch.float8_e4m3fn)``, ``run_poc.py:81-134``).  This restates the same
+# placement token by token into a block pool addressed through a block table,
+# using ``owner_and_local_position`` (``layout.py:10-16``) for each token.
+# ----------------------------------------------------------------------------
+
+def cache_write(pool: np.ndarray, table: np.ndarray, k_seq: np.ndarray, v_seq: np.ndarray, first: int,
+                cfg: OracleConfig, rank: int, kv_is_bf16: bool) -> None:
+    """Write the tokens of ``k_seq``/``v_seq`` (``[Hkv, T, D]`` fp32 holding
+    bf16 values, token t at absolute position ``first + t``) that ``rank``
+    owns into ``pool`` (uint8 ``[pool_blocks, payload_bytes]``, packed payload
+    layout ``[2][Hkv][bs][D]`` per block), in place.  FP8 codes come from
+    ``e4m3fn_encode``; bf16 is stored as its bit pattern (little endian)."""
+    hkv, T, dim = k_seq.shape
+    bs = cfg.block_size
+    elt = 2 if kv_is_bf16 else 1
+    view = pool.reshape(pool.shape[0], 2, hkv, bs, dim * elt)
+    pos = first + np.arange(T, dtype=np.int64)
+    stride = cfg.pcp_size * cfg.interleave_size
+    owner = (pos // cfg.interleave_size) % cfg.pcp_size
+    local = (pos // stride) * cfg.interleave_size + pos % cfg.interleave_size
+    mine = np.nonzero(owner == rank)[0]
+    for t in mine:  # per token: the same (owner, local) as owner_and_local_position
+        assert owner_and_local_position(int(pos[t]), cfg.pcp_size, cfg.interleave_size) == (rank, int(local[t]))
+    blk, row = local[mine] // bs, local[mine] % bs
+    phys = np.asarray(table)[blk]
+    for kv, src in ((0, k_seq), (1, v_seq)):
+        vals = np.ascontiguousarray(src[:, mine, :].transpose(1, 0, 2), dtype=np.float32)  # [n, Hkv, D]
+        if kv_is_bf16:
+            enc = (vals.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).reshape(len(mine), hkv, dim * 2)
+        else:
+            enc = e4m3fn_encode(vals)
+        view[phys, kv, :, row, :] = enc

@@ -13,7 +13,13 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from aws_training_study_b200.pcp_attention import PCPAttentionConfig, pack_local_kv, shard_history, shard_query
+from aws_training_study_b200.pcp_attention import (
+    PCPAttentionConfig,
+    global_positions_for_rank,
+    pack_local_kv,
+    shard_history,
+    shard_query,
+)
 from aws_training_study_b200.pcp_attention.inputs import make_baseline_inputs
 from oracle import pcp_oracle as orc
 
@@ -97,3 +103,24 @@ def assert_parity(actual: torch.Tensor, expected: np.ndarray, label: str = "") -
     assert m["rel_l2"] <= REL_L2, f"{label}: rel-L2 {m}"
     assert m["norm_ratio"] >= 0.25, f"{label}: output trivially small {m}"
     return m
+
+
+def make_current(cfg: PCPAttentionConfig, seed: int, scale: float = 0.5):
+    """Current (prefill) tokens' K/V in sequence order ``[Hkv, current_len, D]``
+    bf16 (seeded N(0, scale^2)) and their striped per-rank shards (the
+    ``shard_query`` layout)."""
+    g = torch.Generator().manual_seed(seed + 7919)
+    shape = (cfg.num_kv_heads, cfg.current_len, cfg.head_dim)
+    k_cur = (torch.randn(shape, generator=g) * scale).to(torch.bfloat16)
+    v_cur = (torch.randn(shape, generator=g) * scale).to(torch.bfloat16)
+    pos = [global_positions_for_rank(cfg.current_len, r, cfg.pcp_size, cfg.interleave_size) for r in range(cfg.pcp_size)]
+    return k_cur, v_cur, [k_cur[:, p].contiguous() for p in pos], [v_cur[:, p].contiguous() for p in pos]
+
+
+def expected_prefill_output(cfg: PCPAttentionConfig, q, k, v, k_cur, v_cur, rank: int) -> np.ndarray:
+    """Oracle prefill output of one rank: its Q shard over the whole history
+    and, causally, the current tokens."""
+    oc = oracle_config(cfg)
+    q_shard = orc.shard_query(to_numpy_f32(q), oc)[rank]
+    return orc.prefill_attention(q_shard, to_numpy_f32(k), to_numpy_f32(v), to_numpy_f32(k_cur),
+                                 to_numpy_f32(v_cur), oc, rank)

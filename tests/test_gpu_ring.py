@@ -60,11 +60,87 @@ def ring_ragged_allgather(rank, world):
     return _ring_body(rank, world, "ragged_d128_bf16", exchange="allgather")
 
 
+def prefill_ragged(rank, world):
+    """History plus causal current tokens through the handle: the current
+    K/V shards are all-gathered inside the C ABI."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from aws_training_study_b200.pcp_attention import PCPAttentionConfig
+    from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
+    from parity import assert_parity, expected_prefill_output, make_case, make_current, packed_shards
+
+    P, cur, mh, ah, bs, I, hq, hkv, d, kv = CASES["ragged_d128_bf16"]
+    cfg = PCPAttentionConfig(P, cur, mh, ah, bs, I, hq, hkv, d).validate()
+    torch.cuda.set_device(rank)
+    q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=13, kv_dtype=torch.bfloat16)
+    k_cur, v_cur, kc_shards, vc_shards = make_current(cfg, seed=13)
+    packed = packed_shards(cfg, k_shards, v_shards)
+    attn = HistoryAttention(cfg, kv_dtype=torch.bfloat16, rank=rank, device=rank)
+    qd, kvd = q_shards[rank].cuda(), packed[rank].cuda()
+    kcd, vcd = kc_shards[rank].cuda(), vc_shards[rank].cuda()
+    for _ in range(2):
+        out = attn.prefill(qd, kvd, kcd, vcd)
+    attn.status(120000)
+    st = attn.stats()
+    m = assert_parity(out, expected_prefill_output(cfg, q, k, v, k_cur, v_cur, rank), f"prefill rank {rank}")
+    attn.close()
+    return {"metrics": m, "ring_bytes": st["ring_bytes"], "attn_launches": st["attn_launches"]}
+
+
+def ring_paged(rank, world):
+    """Each rank's cache written by the GPU producer into a pool through a
+    permuted block table, then attended through the handle's paged entry
+    (its live blocks are gathered before the exchange)."""
+    import sys
+    from pathlib import Path
+
+    import numpy as np
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from aws_training_study_b200.pcp_attention import PCPAttentionConfig
+    from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
+    from aws_training_study_b200.pcp_attention.paged import cache_write, make_pool
+    from oracle import pcp_oracle as orc
+    from parity import assert_parity, oracle_config, to_numpy_f32
+
+    P, cur, mh, ah, bs, I, hq, hkv, d, kv = CASES["qwen_d256_fp8"]
+    ah = 7000  # ragged: the ranks hold different block counts
+    cfg = PCPAttentionConfig(P, cur, mh, ah, bs, I, hq, hkv, d).validate()
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(hq, cur, d, generator=g).to(torch.bfloat16)
+    k = (torch.randn(hkv, ah, d, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(hkv, ah, d, generator=g) * 0.5).to(torch.bfloat16)
+    nb = cfg.max_local_blocks
+    table = torch.from_numpy(np.random.default_rng(rank).permutation(nb + 4)[:nb].astype(np.int32)).to(dev)
+    pool = make_pool(cfg, nb + 4, torch.float8_e4m3fn, dev)
+    st = cache_write(cfg, rank, 0, k.to(dev), v.to(dev), table, pool)
+    assert int(st.item()) == 0
+    oc = oracle_config(cfg)
+    q_shard = torch.from_numpy(orc.shard_query(to_numpy_f32(q), oc)[rank]).to(torch.bfloat16).to(dev)
+    attn = HistoryAttention(cfg, rank=rank, device=rank)
+    for _ in range(2):
+        out = attn.forward_paged(q_shard, pool, table)
+    attn.status(120000)
+    stats = attn.stats()
+    kq = orc.e4m3fn_decode(orc.e4m3fn_encode(to_numpy_f32(k)))
+    vq = orc.e4m3fn_decode(orc.e4m3fn_encode(to_numpy_f32(v)))
+    want = orc.dense_history_attention(to_numpy_f32(q_shard), kq, vq, oc.softmax_scale)
+    m = assert_parity(out, want, f"paged rank {rank}")
+    attn.close()
+    return {"metrics": m, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather"])
+@pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather",
+                                "prefill_ragged", "ring_paged"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res
     for rank, (status, payload) in res.items():
         assert status == "ok", payload
-        assert payload["ring_bytes"] > 0 and payload["attn_launches"] == 2
+        # local shard, remote shard (+ the causal current-token launch)
+        assert payload["ring_bytes"] > 0 and payload["attn_launches"] == (3 if fn == "prefill_ragged" else 2)
