@@ -86,6 +86,7 @@ SIGNATURES = {
     "pcp_prefill_attention": (_c.c_int, [_PDIMS, _I32, _I32, _P, _P, _I32, _PI32, _P, _P, _P, _P, _c.c_size_t, _P]),
     "pcp_create": (_c.c_int, [_PDIMS, _I32, _I32, _P, _c.POINTER(_P)]),
     "pcp_forward": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_forward_bucketed": (_c.c_int, [_P, _P, _P, _P, _PI32, _P, _P]),
     "pcp_forward_paged": (_c.c_int, [_P, _P, _P, _c.c_int64, _P, _PI32, _P, _P]),
     "pcp_forward_prefill": (_c.c_int, [_P, _I32, _P, _P, _PI32, _P, _P, _P, _P]),
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),

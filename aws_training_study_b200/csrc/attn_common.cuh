@@ -64,6 +64,7 @@ enum : int {
   kErrSmemAlign = 107,
   kErrWaitRed = 108,
   kErrBlockTable = 109,  // a block-table entry outside the pool (nothing written or read there)
+  kErrBucket = 110,      // a device valid length above its bucket's bound (clamped to the bound)
 };
 
 struct AttnParams {
@@ -90,6 +91,10 @@ struct AttnParams {
   int stripe_ranks;      // P
   int stripe_width;      // I
   int stripe_rank;       // rank of the query shard
+  // Device-length mode: the valid keys are *num_keys_dev (written by the
+  // unpack of this part; at most num_keys, the bucket's bound).  Splits past
+  // them are empty: they store lse = -inf so the combine ignores them.
+  const int* num_keys_dev;
 };
 
 // Global position of local query/key index i of `rank`'s striped shard

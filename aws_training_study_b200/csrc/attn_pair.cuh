@@ -91,7 +91,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pt = pair % p.m_tiles_per_head;
   const int row0 = pt * kPairRows + static_cast<int>(rank) * kTileM;  // first query row of this CTA
   const int split = blockIdx.y;
-  int n_key_tiles = (p.num_keys + kTileN - 1) / kTileN;
+  const int num_keys = p.num_keys_dev ? min(max(*p.num_keys_dev, 0), p.num_keys) : p.num_keys;
+  int n_key_tiles = (num_keys + kTileN - 1) / kTileN;
   if (p.causal) {
     // Last key tile any of the pair's 256 rows can see (rows past the end
     // are padding; a tile that wraps into the next Q head holds Qloc - 1).
@@ -103,7 +104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   const int kt0 = split * p.tiles_per_split;
   const int kt1 = min(kt0 + p.tiles_per_split, n_key_tiles);
-  const int n = kt1 - kt0;  // >= 1 by construction on the host
+  const int n = kt1 - kt0;  // >= 1 on the host plan; <= 0 only for an empty split in device-length mode
 
   if (warp == kProducerWarp && lane == 0) {
     mbar_init(bar_q, 1);
@@ -251,7 +252,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     // Keys this row may see: all valid keys, or (causal) those up to its own
     // global position -- at least key 0, so the first tile is never empty.
-    int key_limit = p.num_keys;
+    int key_limit = num_keys;
     if (p.causal)
       key_limit = min(key_limit, striped_position((row0 + row) % p.q_local_len, p.stripe_ranks, p.stripe_width,
                                                   p.stripe_rank) + 1);
@@ -419,6 +420,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (live && wg == 0) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
       }
+    } else if (n <= 0 && !p.write_final && wg == 0) {
+      // Empty split (device-length mode): weight zero in the combine.
+      const int rih = row0 + row;
+      if (rih < p.rows_per_head)
+        p.part_lse[static_cast<size_t>(p.split_base + split) * p.total_rows +
+                   static_cast<size_t>(head) * p.rows_per_head + rih] = -INFINITY;
     }
   }
 

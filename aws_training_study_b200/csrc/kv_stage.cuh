@@ -30,8 +30,9 @@ struct UnpackSource {
   const uint8_t* base;   // first block of this source's packed payload (or the block pool)
   const int32_t* table;  // NULL: blocks are contiguous; else logical block -> pool block (device)
   long long pool_blocks; // blocks the pool holds (checked when `table` is set)
-  int valid;             // valid tokens of this source
-  int dst_offset;        // first key slot in the dense output
+  int valid;             // valid tokens of this source (device-length mode: the bucket's upper bound)
+  int dst_offset;        // first key slot in the dense output (device-length mode: the part's first key)
+  int dev_index;         // device-length mode: index of this source in UnpackParams::valid_dev
 };
 
 struct UnpackParams {
@@ -45,7 +46,19 @@ struct UnpackParams {
   __nv_bfloat16* k_out;
   __nv_bfloat16* v_out;
   int* err;                  // set to kErrBlockTable on an entry outside the pool
+  // Device-length mode (valid_dev != NULL, bucketed graphs): the valid count
+  // of source s is valid_dev[src[s].dev_index], clamped to src[s].valid (a
+  // larger one records kErrBucket); sources are compacted in order from
+  // their common dst_offset, and block (0, 0) stores the part's total keys
+  // in *part_keys for the attention launch that follows.
+  const int32_t* valid_dev;
+  int* part_keys;
 };
+
+__device__ __forceinline__ int device_valid(const UnpackParams& p, int s) {
+  const int v = p.valid_dev[p.src[s].dev_index];
+  return min(max(v, 0), p.src[s].valid);
+}
 
 __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
   const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
@@ -57,7 +70,18 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
 // converts 16 consecutive head-dim elements of one token of one head.
 __global__ void __launch_bounds__(256) kv_unpack_kernel(const UnpackParams p) {
   const int s = blockIdx.y;
-  const UnpackSource src = p.src[s];
+  UnpackSource src = p.src[s];
+  if (p.valid_dev) {
+    const int v = p.valid_dev[src.dev_index];
+    if ((v < 0 || v > src.valid) && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(p.err, 0, kErrBucket);
+    for (int i = 0; i < s; ++i) src.dst_offset += device_valid(p, i);
+    src.valid = device_valid(p, s);
+    if (blockIdx.x == 0 && s == 0 && threadIdx.x == 0) {
+      int total = 0;
+      for (int i = 0; i < p.num_sources; ++i) total += device_valid(p, i);
+      *p.part_keys = total;
+    }
+  }
   const int chunks_per_row = p.head_dim / 16;
   const int live_blocks = (src.valid + p.block_size - 1) / p.block_size;
   const long long per_block = 2LL * p.num_kv_heads * p.block_size * chunks_per_row;
@@ -287,6 +311,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     for (int i = 0; i < per_lane; ++i) acc[i] = 0.f;
     for (int s = 0; s < p.num_splits; ++s) {
       const float ws = __shfl_sync(0xffffffffu, w, s);
+      if (ws == 0.f) continue;  // an empty split (lse = -inf): its O was never written
       const float* src = p.part_o + (static_cast<size_t>(s) * p.rows + row) * D + lane * per_lane;
 #pragma unroll
       for (int i = 0; i < per_lane; i += 4) {

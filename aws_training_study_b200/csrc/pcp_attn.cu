@@ -134,12 +134,19 @@ int check_dims(const pcp_dims_t* d) {
   return PCP_OK;
 }
 
-pcp::UnpackSource contiguous_src(const void* base, int valid, int64_t dst_offset) {
-  return {static_cast<const uint8_t*>(base), nullptr, 0, valid, static_cast<int>(dst_offset)};
+pcp::UnpackSource contiguous_src(const void* base, int valid, int64_t dst_offset, int dev_index = -1) {
+  return {static_cast<const uint8_t*>(base), nullptr, 0, valid, static_cast<int>(dst_offset), dev_index};
 }
-pcp::UnpackSource paged_src(const void* pool, const int32_t* table, int64_t pool_blocks, int valid, int64_t dst_offset) {
-  return {static_cast<const uint8_t*>(pool), table, pool_blocks, valid, static_cast<int>(dst_offset)};
+pcp::UnpackSource paged_src(const void* pool, const int32_t* table, int64_t pool_blocks, int valid, int64_t dst_offset,
+                            int dev_index = -1) {
+  return {static_cast<const uint8_t*>(pool), table, pool_blocks, valid, static_cast<int>(dst_offset), dev_index};
 }
+
+// Device-length mode: per-part valid key counts written by the unpack, in
+// the workspace header (after the error word).
+constexpr size_t kPartKeysOff = 64;
+constexpr int kMaxParts = 8;
+int* part_keys_slot(uint8_t* ws, int part) { return reinterpret_cast<int*>(ws + kPartKeysOff) + part; }
 
 int64_t payload_bytes(const pcp_dims_t& d) {
   return 2LL * d.num_kv_heads * d.block_size * d.head_dim * (d.kv_dtype == PCP_KV_BF16 ? 2 : 1);
@@ -206,7 +213,8 @@ struct LaunchCounter {
 };
 
 int launch_unpack(const pcp_dims_t& d, const std::vector<pcp::UnpackSource>& srcs, const Workspace& w, uint8_t* ws,
-                  cudaStream_t st, LaunchCounter* lc) {
+                  cudaStream_t st, LaunchCounter* lc, const int32_t* valid_dev = nullptr,
+                  int* part_keys = nullptr) {
   if (srcs.empty()) return PCP_OK;
   if (srcs.size() > static_cast<size_t>(pcp::kMaxSources)) return fail(PCP_ERR_UNSUPPORTED, "too many sources");
   pcp::UnpackParams p{};
@@ -226,6 +234,8 @@ int launch_unpack(const pcp_dims_t& d, const std::vector<pcp::UnpackSource>& src
   p.k_out = reinterpret_cast<__nv_bfloat16*>(ws + w.k_off);
   p.v_out = reinterpret_cast<__nv_bfloat16*>(ws + w.v_off);
   p.err = reinterpret_cast<int*>(ws);
+  p.valid_dev = valid_dev;
+  p.part_keys = part_keys;
   const int64_t live_blocks = ceil_div(max_valid, d.block_size);
   const int64_t items = live_blocks * 2 * d.num_kv_heads * d.block_size * (d.head_dim / 16);
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 4 * 148));
@@ -247,7 +257,8 @@ struct Causal {
 // workspace K/V.  Writes bf16 `out` directly (final) or split partials.
 int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uint8_t* ws, int64_t key_off,
                      int64_t num_keys, const SplitPlan& plan, int split_base, bool final_out, void* out,
-                     cudaStream_t st, LaunchCounter* lc, const Causal& causal = Causal{}) {
+                     cudaStream_t st, LaunchCounter* lc, const Causal& causal = Causal{},
+                     const int* num_keys_dev = nullptr) {
   const int64_t R = rows_per_head(d);
   const int64_t mt = ceil_div(R, pcp::kPairRows);  // CTA-pair tiles per KV head
   CUtensorMap tq, tk, tv, to;
@@ -275,6 +286,7 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   p.stripe_ranks = d.pcp_size;
   p.stripe_width = std::max(1, causal.stripe_width);
   p.stripe_rank = causal.rank;
+  p.num_keys_dev = num_keys_dev;
   // Two CTAs (one cluster) per pair tile; the cluster shape is compiled in.
   dim3 grid(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
   if (d.head_dim == 256) {
@@ -508,11 +520,31 @@ int launch_block_gather(const pcp_dims_t& d, const LocalKV& local, int live_bloc
 // k_cur / v_cur (optional, both or neither): this rank's current tokens'
 // K/V shard [Hkv][Qloc][D] bf16, striped like Q with `stripe_width`; they are
 // gathered from every rank and attended causally as one more split.
+// Restores the handle's profiling switch on scope exit (forwards recorded
+// into a CUDA graph take no profiling spans).
+struct ProfilingOff {
+  pcp_handle* h;
+  bool saved;
+  ProfilingOff(pcp_handle* hh, bool off) : h(hh), saved(hh->profiling) {
+    if (off) h->profiling = false;
+  }
+  ~ProfilingOff() { h->profiling = saved; }
+};
+
+// valid_dev (optional, device int32[P]): device-length mode.  valid_len then
+// holds each source's upper bound (the bucket): transfers, key regions,
+// split plans and grids are sized by the bounds, while the kernels read the
+// actual counts from valid_dev -- so one CUDA graph recorded for a bucket
+// serves every length inside it and still skips every tile past them.
 int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32_t* valid_len, const void* k_cur,
-                 const void* v_cur, int stripe_width, void* out, cudaStream_t st) {
+                 const void* v_cur, int stripe_width, void* out, cudaStream_t st,
+                 const int32_t* valid_dev = nullptr) {
   const pcp_dims_t& d = h->d;
   const int P = d.pcp_size;
   const int r = h->rank;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  CUDA_TRY(cudaStreamIsCapturing(st, &capture));
+  ProfilingOff prof_guard(h, capture != cudaStreamCaptureStatusNone);
   if (!q || !local.base || !valid_len || !out) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
   if (local.table && local.pool_blocks <= 0) return fail(PCP_ERR_INVALID_ARGUMENT, "empty block pool");
   const bool with_cur = k_cur != nullptr || v_cur != nullptr;
@@ -545,8 +577,9 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   parts[0].key_off = 0;
   parts[0].keys = valid_len[r];
   if (valid_len[r] > 0)
-    parts[0].srcs.push_back(local.table ? paged_src(local.base, local.table, local.pool_blocks, valid_len[r], 0)
-                                        : contiguous_src(local.base, valid_len[r], 0));
+    parts[0].srcs.push_back(local.table
+                                ? paged_src(local.base, local.table, local.pool_blocks, valid_len[r], 0, r)
+                                : contiguous_src(local.base, valid_len[r], 0, r));
   int64_t next_key = parts[0].keys;
   int64_t sent = 0;
   // Cleared before the ring stream starts: its block gather may report too.
@@ -592,7 +625,8 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       for (int step = s0; step < s1; ++step) {
         const int src = ((r - step) % P + P) % P;
         if (valid_len[src] > 0)
-          part.srcs.push_back(contiguous_src(slot(src), valid_len[src], part.key_off + part.keys));
+          part.srcs.push_back(valid_dev ? contiguous_src(slot(src), valid_len[src], part.key_off, src)
+                                        : contiguous_src(slot(src), valid_len[src], part.key_off + part.keys));
         part.keys += valid_len[src];
       }
       next_key += part.keys;
@@ -685,6 +719,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   }
   if (with_cur) ++total_splits;
   const bool direct = total_splits == 1;
+  if (parts.size() > static_cast<size_t>(kMaxParts)) return fail(PCP_ERR_UNSUPPORTED, "too many parts");
   int split_base = 0;
   // Current tokens: scatter every rank's shard into sequence order after the
   // history keys, then one causal launch.
@@ -706,12 +741,13 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     if (ready[i]) CUDA_TRY(cudaStreamWaitEvent(st, ready[i], 0));
     const Part& part = parts[i];
     if (!part.keys) continue;
+    int* keys_dev = valid_dev ? part_keys_slot(h->ws, static_cast<int>(i)) : nullptr;
     int sp = prof_begin(h, 1, st);
-    PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc));
+    PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc, valid_dev, keys_dev));
     prof_end(h, sp, st);
     sp = prof_begin(h, 2, st);
     PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, direct, out, st,
-                             &lc));
+                             &lc, Causal{}, keys_dev));
     prof_end(h, sp, st);
     split_base += part.plan.splits;
   }
@@ -1147,6 +1183,17 @@ int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int
   LocalKV local;
   local.base = packed_kv;
   return forward_impl(h, q, local, valid_len, nullptr, nullptr, 0, out, static_cast<cudaStream_t>(stream));
+}
+
+int pcp_forward_bucketed(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len_dev,
+                         const int32_t* bucket_len, void* out, void* stream) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (h->comm_failed) return fail(PCP_ERR_PEER, "the ring communicator was aborted");
+  if (!valid_len_dev || !bucket_len) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL valid_len_dev or bucket_len");
+  LocalKV local;
+  local.base = packed_kv;
+  return forward_impl(h, q, local, bucket_len, nullptr, nullptr, 0, out, static_cast<cudaStream_t>(stream),
+                      valid_len_dev);
 }
 
 int pcp_forward_paged(pcp_handle_t* h, const void* q, const void* cache_pool, int64_t pool_blocks,

@@ -205,6 +205,31 @@ class HistoryAttention:
             )
         return out
 
+    def forward_bucketed(self, q: torch.Tensor, packed_kv: torch.Tensor, valid_dev: torch.Tensor, bucket_len,
+                         out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """``__call__`` whose valid lengths are read on the device from
+        ``valid_dev`` (int32 ``[P]``) when the kernels run; ``bucket_len`` (P
+        ints) bounds them and sizes every transfer and launch.  This is the
+        call a length-bucket CUDA graph records (``graphs.BucketGraph``)."""
+        self._check_inputs(q, packed_kv)
+        if valid_dev.dtype != torch.int32 or valid_dev.numel() != self.config.pcp_size or \
+                valid_dev.device != self.device or not valid_dev.is_contiguous():
+            raise ValueError(f"valid_dev must be a contiguous int32 [{self.config.pcp_size}] tensor on {self.device}")
+        if out is None:
+            out = torch.empty_like(q)
+        elif tuple(out.shape) != tuple(q.shape) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous bf16 tensor shaped like q")
+        bounds = self._valid(bucket_len)
+        with torch.cuda.device(self.device):
+            _capi.check(
+                _capi.lib().pcp_forward_bucketed(
+                    self._handle, ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(packed_kv.data_ptr()),
+                    ctypes.c_void_p(valid_dev.data_ptr()), bounds, ctypes.c_void_p(out.data_ptr()),
+                    _cuda_stream_ptr(stream)
+                )
+            )
+        return out
+
     def forward_paged(self, q: torch.Tensor, pool: torch.Tensor, block_table: torch.Tensor, valid_len=None,
                       out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """``__call__`` with this rank's history shard in a block pool
@@ -293,7 +318,17 @@ class HistoryAttention:
         _capi.check(_capi.lib().pcp_get_stats(self._handle, ctypes.byref(st)))
         return {name: getattr(st, name) for name, _ in _capi.PcpStats._fields_}
 
+    def _register_graph(self, graph) -> None:
+        import weakref
+
+        if not hasattr(self, "_graphs"):
+            self._graphs = weakref.WeakSet()
+        self._graphs.add(graph)
+
     def close(self) -> None:
+        # Graphs that recorded this handle's NCCL calls go before the communicator.
+        for g in list(getattr(self, "_graphs", ())):
+            g.reset()
         if getattr(self, "_handle", None) is not None and self._handle.value:
             _capi.lib().pcp_destroy(self._handle)
             self._handle = ctypes.c_void_p()

@@ -231,6 +231,21 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
 int pcp_forward(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len, void* out,
                 void* stream);
 
+/* Length buckets (README.md:52-54: one artifact per bucket, masked blocks
+ * skipped).  pcp_forward whose valid lengths are read ON THE DEVICE from
+ * valid_len_dev (DEVICE int32[P]) when the kernels run, while everything the
+ * host plans -- NCCL transfer sizes, key regions, split plans, grids -- is
+ * sized by bucket_len (HOST int32[P], each source's upper bound).  Recorded
+ * into a CUDA graph (stream capture of this call), one graph serves every
+ * valid_len <= bucket_len: the caller writes new lengths into valid_len_dev
+ * and replays.  Per source: blocks past bucket_len are never sent, unpacked
+ * or computed; blocks between valid_len and bucket_len are sent (the bucket's
+ * slack) but never unpacked or computed.  A device length above its bound is
+ * clamped and reported as code 110 by pcp_device_status.  The total of
+ * valid_len_dev must be positive (else the output is unspecified). */
+int pcp_forward_bucketed(pcp_handle_t* h, const void* q, const void* packed_kv, const int32_t* valid_len_dev,
+                         const int32_t* bucket_len, void* out, void* stream);
+
 /* pcp_forward with this rank's shard in a paged cache: its logical block b is
  * pool block block_table[b] (DEVICE int32[max_local_blocks]) of cache_pool
  * [pool_blocks][payload].  The live blocks are gathered into a contiguous

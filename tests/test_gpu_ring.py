@@ -134,9 +134,46 @@ def ring_paged(rank, world):
     return {"metrics": m, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
 
 
+def ring_graph(rank, world):
+    """A length-bucket CUDA graph that records the NCCL exchange, replayed
+    for several history lengths inside its bucket."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from aws_training_study_b200.pcp_attention import PCPAttentionConfig
+    from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
+    from aws_training_study_b200.pcp_attention.graphs import BucketGraph, bucket_for
+    from oracle import pcp_oracle as orc
+    from parity import assert_parity, make_case, oracle_config, packed_shards, to_numpy_f32
+
+    P, cur, mh, ah, bs, I, hq, hkv, d, kv = CASES["qwen_d256_fp8"]
+    cfg = PCPAttentionConfig(P, cur, mh, ah, bs, I, hq, hkv, d).validate()
+    torch.cuda.set_device(rank)
+    q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=19)
+    packed = packed_shards(cfg, k_shards, v_shards)
+    attn = HistoryAttention(cfg, rank=rank, device=rank)
+    qd, kvd = q_shards[rank].cuda(), packed[rank].cuda()
+    lens = {h: [orc.source_valid_len(h, P, I, s) for s in range(P)] for h in (6000, 5121, 4100)}
+    bucket = bucket_for(cfg, lens[6000], granularity_blocks=2)
+    g = BucketGraph(attn, bucket, qd, kvd)
+    oc = oracle_config(cfg)
+    q_shard = orc.shard_query(to_numpy_f32(q), oc)[rank]
+    worst = {}
+    for hist, vl in lens.items():
+        out = g.replay(vl).clone()
+        attn.status(120000)
+        want = orc.dense_history_attention(q_shard, to_numpy_f32(k[:, :hist]), to_numpy_f32(v[:, :hist]),
+                                           oc.softmax_scale)
+        worst[hist] = assert_parity(out, want, f"graph rank {rank} hist {hist}")
+    stats = attn.stats()
+    attn.close()
+    return {"metrics": worst, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather",
-                                "prefill_ragged", "ring_paged"])
+                                "prefill_ragged", "ring_paged", "ring_graph"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res

@@ -215,3 +215,16 @@ def test_input_generators_bit_exact_with_reference():
     tiny = get_preset("tiny")
     assert [sha(t) for t in make_inputs(tiny, 1234)] == [str(x) for x in g["make_inputs_sha"]]
     assert [sha(t) for t in make_local_inputs(tiny, 1234, 1)] == [str(x) for x in g["make_local_inputs_sha"]]
+
+
+def test_bucket_for_rounds_up_to_block_groups_and_caps():
+    from aws_training_study_b200.pcp_attention.graphs import bucket_for
+
+    cfg = PCPAttentionConfig(2, 256, 8192, 8192, 512, 64, 4, 2, 128)  # 8 blocks per shard
+    assert bucket_for(cfg, [0, 1], 2) == (0, 1024)
+    assert bucket_for(cfg, [1024, 1025], 2) == (1024, 2048)
+    assert bucket_for(cfg, [4000, 4096], 3) == (4096, 4096)  # capped at the shard capacity
+    with pytest.raises(ValueError):
+        bucket_for(cfg, [4097, 0], 1)
+    with pytest.raises(ValueError):
+        bucket_for(cfg, [1, 1], 0)
