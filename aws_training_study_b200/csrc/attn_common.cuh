@@ -65,6 +65,7 @@ enum : int {
   kErrWaitRed = 108,
   kErrBlockTable = 109,  // a block-table entry outside the pool (nothing written or read there)
   kErrBucket = 110,      // a device valid length above its bucket's bound (clamped to the bound)
+  kErrSchedule = 111,    // a segment's partial slot beyond the launch's slot count (not written)
 };
 
 struct AttnParams {
@@ -76,7 +77,8 @@ struct AttnParams {
   int split_base;        // first split index of this launch in the partial buffers
   int total_rows;        // num_kv_heads * R
   float scale_log2;      // softmax_scale * log2(e)
-  int write_final;       // 1: bf16 O via TMA; 0: fp32 partial O + lse
+  int write_final;       // static schedule: 1 bf16 O, 0 fp32 partial O + lse
+  __nv_bfloat16* out;    // bf16 O [total_rows][D]
   float* part_o;         // [splits][total_rows][D]
   float* part_lse;       // [splits][total_rows]
   int* err;              // device error word
@@ -95,7 +97,26 @@ struct AttnParams {
   // unpack of this part; at most num_keys, the bucket's bound).  Splits past
   // them are empty: they store lse = -inf so the combine ignores them.
   const int* num_keys_dev;
+  // Stream-K instantiation: partial slots [split_base, split_base +
+  // max_segs) per unit; a unit that one segment covers is written as bf16 O
+  // when final_ok.  (Static: unit = pair, split = blockIdx.y, bf16 O when
+  // write_final.)
+  int max_segs;
+  int final_ok;
 };
+
+// Stream-K partition of T (unit, key tile) steps over G pairs: pair g owns
+// steps [T g / G, T (g + 1) / G).  At least two steps per pair, so a unit of a
+// launch with U units is cut into at most ceil(2G/U) + 1 segments.
+__host__ __device__ __forceinline__ long long stream_k_pairs(long long steps, int grid_pairs) {
+  const long long half = steps / 2;
+  const long long g = grid_pairs < half ? grid_pairs : half;
+  return g > 1 ? g : 1;
+}
+// The pair whose range holds step x.
+__host__ __device__ __forceinline__ long long stream_k_pair_of(long long x, long long steps, long long pairs) {
+  return ((x + 1) * pairs + steps - 1) / steps - 1;
+}
 
 // Global position of local query/key index i of `rank`'s striped shard
 // (pcp_attention/layout.py:19-31).

@@ -287,14 +287,33 @@ struct CombineParams {
   __nv_bfloat16* out;     // [rows][D]
   int num_splits;         // <= 32
   int rows;
+  // Single-part stream-K launch: the attention kernel wrote the rows of every
+  // unit that one segment covered as final output; those rows are skipped.
+  int skip_single;
+  int units, grid_pairs, rows_per_head, m_tiles;
+  int num_keys;              // key count of the launch (or its bound)
+  const int* num_keys_dev;   // device-length mode: the actual count
 };
 
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int warps_per_block = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
+  long long n_kt = 0, steps = 0, pairs = 1;
+  if (p.skip_single) {
+    const int keys = p.num_keys_dev ? min(max(*p.num_keys_dev, 0), p.num_keys) : p.num_keys;
+    n_kt = (keys + kTileN - 1) / kTileN;
+    steps = static_cast<long long>(p.units) * n_kt;
+    pairs = stream_k_pairs(steps, p.grid_pairs);
+  }
   for (int row = blockIdx.x * warps_per_block + (threadIdx.x >> 5); row < p.rows;
        row += gridDim.x * warps_per_block) {
+    if (p.skip_single && steps > 0) {
+      const long long unit =
+          static_cast<long long>(row / p.rows_per_head) * p.m_tiles + (row % p.rows_per_head) / (2 * kTileM);
+      const long long ub = unit * n_kt;
+      if (stream_k_pair_of(ub + n_kt - 1, steps, pairs) == stream_k_pair_of(ub, steps, pairs)) continue;
+    }
     const float lse = lane < p.num_splits ? p.part_lse[static_cast<size_t>(lane) * p.rows + row] : -INFINITY;
     float m = lse;
 #pragma unroll

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "attn_pair.cuh"
+#include "attn_pair_sk.cuh"
 #include "kv_stage.cuh"
 
 namespace {
@@ -87,26 +88,50 @@ int make_tmap(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, u
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
 
+// Attention schedules (AttnParams::stream_k).
+constexpr int kModeStatic = 0;   // one (unit, key split) item per CTA pair, in waves
+constexpr int kModeStreamK = 1;  // equal contiguous (unit, tile) ranges per persistent pair
+// Stream-K only while the launch's bf16 K/V stays well inside the 126 MB L2
+// (its pairs read K/V at unrelated offsets).
+constexpr int64_t kStreamKMaxKvBytes = int64_t(48) << 20;
+
 struct SplitPlan {
-  int splits = 1;
-  int tiles_per_split = 1;
+  int splits = 1;           // partial slots per unit the launch may write
+  int tiles_per_split = 1;  // static: key tiles per split
+  int mode = kModeStatic;
+  int pairs = 1;            // stream-K: CTA pairs in the grid
 };
 
-// Choose how many key splits a launch uses so that (work units) fill whole
-// waves of the SMs.  A work unit is a CTA pair (two SMs).  Cost model:
-// waves * (tiles per unit + 2 tiles of fixed prologue/epilogue cost), with a
-// small bias against splitting.
-SplitPlan plan_splits(int64_t m_units, int64_t n_kt, int sms, int max_splits) {
+// Stream-K: one CTA pair per two SMs (fewer when there are not two tiles per
+// pair), each pair an equal share of the steps; a unit is then cut into at
+// most min(G, ceil(2G/U) + 1) segments, which must fit `slot_cap` partial
+// slots (fewer pairs when they do not).
+SplitPlan plan_stream_k(int64_t units, int64_t n_kt, int sms, int slot_cap) {
+  SplitPlan pl;
+  pl.mode = kModeStreamK;
+  int64_t g = pcp::stream_k_pairs(std::max<int64_t>(1, units * n_kt), std::max(1, sms / 2));
+  auto segs = [&](int64_t gg) { return std::min<int64_t>(gg, ceil_div(2 * gg, std::max<int64_t>(1, units)) + 1); };
+  while (g > 1 && segs(g) > std::max(1, slot_cap)) --g;
+  pl.pairs = static_cast<int>(g);
+  pl.splits = static_cast<int>(segs(g));
+  return pl;
+}
+
+// Static: key splits chosen so that the (unit, split) items fill whole waves
+// of the SM pairs.  Cost model: waves * (tiles per item + 2 tiles of fixed
+// prologue/epilogue cost), with a small bias against splitting.
+SplitPlan plan_static(int64_t units, int64_t n_kt, int sms, int slot_cap) {
   const int64_t slots = std::max(1, sms / 2);
   SplitPlan best;
+  best.mode = kModeStatic;
   best.splits = 1;
-  best.tiles_per_split = static_cast<int>(n_kt);
+  best.tiles_per_split = static_cast<int>(std::max<int64_t>(1, n_kt));
   double best_cost = 1e300;
-  const int smax = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_splits, n_kt)));
+  const int smax = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(std::max(1, slot_cap), n_kt)));
   for (int s = 1; s <= smax; ++s) {
-    const int64_t tps = ceil_div(n_kt, s);
-    const int64_t s_eff = ceil_div(n_kt, tps);
-    const int64_t waves = ceil_div(m_units * s_eff, slots);
+    const int64_t tps = ceil_div(std::max<int64_t>(1, n_kt), s);
+    const int64_t s_eff = ceil_div(std::max<int64_t>(1, n_kt), tps);
+    const int64_t waves = ceil_div(units * s_eff, slots);
     const double cost = static_cast<double>(waves) * (static_cast<double>(tps) + 2.0) + (s_eff > 1 ? 0.5 : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
@@ -115,6 +140,17 @@ SplitPlan plan_splits(int64_t m_units, int64_t n_kt, int sms, int max_splits) {
     }
   }
   return best;
+}
+
+int64_t m_units_of(const pcp_dims_t& d);
+
+// The schedule of a history launch over `keys` dense keys (or their bound).
+// `last`: no exchange is in flight while it runs (the forward's last launch).
+SplitPlan plan_splits(const pcp_dims_t& d, int64_t keys, int sms, int slot_cap, bool last) {
+  const int64_t n_kt = std::max<int64_t>(1, ceil_div(keys, pcp::kTileN));
+  const int64_t kv_bytes = keys * d.num_kv_heads * d.head_dim * 4;
+  return last && kv_bytes <= kStreamKMaxKvBytes ? plan_stream_k(m_units_of(d), n_kt, sms, slot_cap)
+                                                : plan_static(m_units_of(d), n_kt, sms, slot_cap);
 }
 
 int check_dims(const pcp_dims_t* d) {
@@ -155,6 +191,7 @@ int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q
 int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
 // Work units of one split: 256-row CTA-pair tiles over every KV head.
 int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kPairRows); }
+int64_t m_units_of(const pcp_dims_t& d) { return m_units(d); }
 
 int num_sms() {
   int dev = 0, sms = 148;
@@ -190,21 +227,34 @@ Workspace ws_layout(const pcp_dims_t& d, int64_t key_cap, int split_cap) {
   return w;
 }
 
-template <int D>
-int set_smem_attr() {
-  static int done = 0;
-  static int status = PCP_OK;
+// Opts a kernel into its dynamic shared memory once per device.
+template <typename Kernel>
+int set_smem_attr(Kernel kernel, int bytes, int* done_mask) {
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(done & (1 << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(pcp::attn_fwd_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pcp::PairSmem<D>::kAlloc);
+  if (!(*done_mask & (1 << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return fail(PCP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    done |= (1 << dev);
+    *done_mask |= (1 << dev);
   }
-  return status;
+  return PCP_OK;
+}
+
+// Static schedule (attn_pair.cuh) or stream-K (attn_pair_sk.cuh).
+template <int D, bool kStreamK>
+int launch_pair_kernel(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
+                       const CUtensorMap& tv, const CUtensorMap& to, const pcp::AttnParams& p) {
+  static int done = 0;
+  if constexpr (kStreamK) {
+    PCP_TRY(set_smem_attr(pcp::attn_fwd_pair_sk_kernel<D>, pcp::PairSmemSK<D>::kAlloc, &done));
+    pcp::attn_fwd_pair_sk_kernel<D><<<grid, pcp::kThreads, pcp::PairSmemSK<D>::kAlloc, st>>>(tq, tk, tv, p);
+  } else {
+    PCP_TRY(set_smem_attr(pcp::attn_fwd_pair_kernel<D>, pcp::PairSmem<D>::kAlloc, &done));
+    pcp::attn_fwd_pair_kernel<D><<<grid, pcp::kThreads, pcp::PairSmem<D>::kAlloc, st>>>(tq, tk, tv, to, p);
+  }
+  return PCP_OK;
 }
 
 struct LaunchCounter {
@@ -277,7 +327,12 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   p.split_base = split_base;
   p.total_rows = static_cast<int>(total_rows(d));
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d.head_dim)) * 1.4426950408889634);
-  p.write_final = final_out ? 1 : 0;
+  // Stream-K decides per unit (final_ok); static writes bf16 O only when
+  // each unit is one item (one split), else every split leaves a partial.
+  p.write_final = (final_out && plan.splits == 1) ? 1 : 0;
+  p.final_ok = final_out ? 1 : 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.max_segs = plan.splits;
   p.part_o = reinterpret_cast<float*>(ws + w.po_off);
   p.part_lse = reinterpret_cast<float*>(ws + w.pl_off);
   p.err = reinterpret_cast<int*>(ws);
@@ -287,14 +342,17 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   p.stripe_width = std::max(1, causal.stripe_width);
   p.stripe_rank = causal.rank;
   p.num_keys_dev = num_keys_dev;
-  // Two CTAs (one cluster) per pair tile; the cluster shape is compiled in.
-  dim3 grid(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
+  // Two CTAs (one cluster) per pair; the cluster shape is compiled in.
+  // Stream-K: a fixed set of pairs; static: one pair per unit and split.
+  const bool sk = plan.mode == kModeStreamK;
+  dim3 grid = sk ? dim3(static_cast<unsigned>(2 * plan.pairs), 1)
+                            : dim3(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
   if (d.head_dim == 256) {
-    PCP_TRY(set_smem_attr<256>());
-    pcp::attn_fwd_pair_kernel<256><<<grid, pcp::kThreads, pcp::PairSmem<256>::kAlloc, st>>>(tq, tk, tv, to, p);
+    PCP_TRY((sk ? launch_pair_kernel<256, true>(grid, st, tq, tk, tv, to, p)
+                : launch_pair_kernel<256, false>(grid, st, tq, tk, tv, to, p)));
   } else {
-    PCP_TRY(set_smem_attr<128>());
-    pcp::attn_fwd_pair_kernel<128><<<grid, pcp::kThreads, pcp::PairSmem<128>::kAlloc, st>>>(tq, tk, tv, to, p);
+    PCP_TRY((sk ? launch_pair_kernel<128, true>(grid, st, tq, tk, tv, to, p)
+                : launch_pair_kernel<128, false>(grid, st, tq, tk, tv, to, p)));
   }
   CUDA_TRY(cudaGetLastError());
   if (lc) {
@@ -348,12 +406,26 @@ SplitPlan causal_plan(const pcp_dims_t& d) {
   SplitPlan pl;
   pl.splits = 1;
   pl.tiles_per_split = static_cast<int>(ceil_div(current_keys(d), pcp::kTileN));
+  pl.mode = kModeStatic;
   return pl;
 }
 
+// `single`: the plan of the only launch, which wrote its single-segment
+// units as final output (rows the combine skips); null when every unit's
+// result is in the partials.
 int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int splits, void* out, cudaStream_t st,
-                   LaunchCounter* lc) {
+                   LaunchCounter* lc, const SplitPlan* single = nullptr, int64_t num_keys = 0,
+                   const int* num_keys_dev = nullptr) {
   pcp::CombineParams p{};
+  if (single) {
+    p.skip_single = 1;
+    p.units = static_cast<int>(m_units(d));
+    p.grid_pairs = single->pairs;
+    p.rows_per_head = static_cast<int>(rows_per_head(d));
+    p.m_tiles = static_cast<int>(ceil_div(rows_per_head(d), pcp::kPairRows));
+    p.num_keys = static_cast<int>(num_keys);
+    p.num_keys_dev = num_keys_dev;
+  }
   p.part_o = reinterpret_cast<const float*>(ws + w.po_off);
   p.part_lse = reinterpret_cast<const float*>(ws + w.pl_off);
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
@@ -376,12 +448,12 @@ struct Part {
   int64_t key_off = 0;
   int64_t keys = 0;
   SplitPlan plan;
+  bool last = true;  // the forward's last history launch (no exchange in flight)
 };
 
 int plan_part(const pcp_dims_t& d, Part* part, int sms, int max_splits) {
-  const int64_t n_kt = ceil_div(part->keys, pcp::kTileN);
-  if (n_kt == 0) return PCP_OK;
-  part->plan = plan_splits(m_units(d), n_kt, sms, max_splits);
+  if (part->keys == 0) return PCP_OK;
+  part->plan = plan_splits(d, part->keys, sms, max_splits, part->last);
   return PCP_OK;
 }
 
@@ -675,9 +747,9 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       // launches and split partials).  Pairs match across ranks: at step s
       // rank r sends to r+s, which receives from (r+s)-s = r in the same group.
       Part probe = parts[0];
+      probe.last = false;
       plan_part(d, &probe, h->sms, max_splits);
-      const bool local_fills_gpu =
-          probe.keys && m_units(d) * probe.plan.splits >= std::max(1, h->sms / 2);
+      const bool local_fills_gpu = probe.keys && probe.plan.pairs >= std::max(1, h->sms / 2);
       const int groups = (P >= 4 && local_fills_gpu) ? 2 : 1;
       const int split_step = 1 + (P - 1 + 1) / 2;
       for (int g = 0; g < groups; ++g) {
@@ -702,6 +774,13 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   // Split plans; keep the total within the partial buffers by shrinking the
   // part with the most splits (the current tokens take one split).
   const int hist_cap = max_splits - (with_cur ? 1 : 0);
+  // Only the last launch that has keys runs with no exchange in flight.
+  int last_live = -1;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    parts[i].last = false;
+    if (parts[i].keys) last_live = static_cast<int>(i);
+  }
+  if (last_live >= 0) parts[last_live].last = true;
   int total_splits = 0;
   for (auto& part : parts) {
     plan_part(d, &part, h->sms, hist_cap);
@@ -713,12 +792,22 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       if (part.keys && (!big || part.plan.splits > big->plan.splits)) big = &part;
     if (!big || big->plan.splits == 1) return fail(PCP_ERR_UNSUPPORTED, "too many launches for the partial buffers");
     const int others = total_splits - big->plan.splits;
-    big->plan = plan_splits(m_units(d), ceil_div(big->keys, pcp::kTileN), h->sms,
-                            std::max(1, std::min(big->plan.splits - 1, hist_cap - others)));
+    big->plan = plan_splits(d, big->keys, h->sms, std::max(1, std::min(big->plan.splits - 1, hist_cap - others)),
+                            big->last);
     total_splits = others + big->plan.splits;
   }
   if (with_cur) ++total_splits;
-  const bool direct = total_splits == 1;
+  int live_parts = 0;
+  const Part* only = nullptr;
+  for (const auto& part : parts)
+    if (part.keys) {
+      ++live_parts;
+      only = &part;
+    }
+  // One history launch and nothing else: it writes its single-segment units
+  // as final output.  Only the current tokens: the causal launch does.
+  const bool single = live_parts == 1 && !with_cur;
+  const bool cur_only = live_parts == 0 && with_cur;
   if (parts.size() > static_cast<size_t>(kMaxParts)) return fail(PCP_ERR_UNSUPPORTED, "too many parts");
   int split_base = 0;
   // Current tokens: scatter every rank's shard into sequence order after the
@@ -730,8 +819,8 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
                            st, &lc));
     prof_end(h, sp, st);
     sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, total, current_keys(d), causal_plan(d), split_base, direct, out, st,
-                             &lc, Causal{r, stripe_width}));
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, total, current_keys(d), causal_plan(d), split_base, cur_only, out,
+                             st, &lc, Causal{r, stripe_width}));
     prof_end(h, sp, st);
     split_base += 1;
     return PCP_OK;
@@ -746,15 +835,19 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc, valid_dev, keys_dev));
     prof_end(h, sp, st);
     sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, direct, out, st,
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, single, out, st,
                              &lc, Causal{}, keys_dev));
     prof_end(h, sp, st);
     split_base += part.plan.splits;
   }
   if (parts.size() == 1 && with_cur) PCP_TRY(launch_current());
-  if (!direct) {
+  if (single ? only->plan.splits > 1 : !cur_only) {
     const int sp = prof_begin(h, 3, st);
-    PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc));
+    const int only_idx = single ? static_cast<int>(only - parts.data()) : 0;
+    const bool skip = single && only->plan.mode == kModeStreamK;
+    PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc, skip ? &only->plan : nullptr,
+                           single ? only->keys : 0,
+                           single && valid_dev ? part_keys_slot(h->ws, only_idx) : nullptr));
     prof_end(h, sp, st);
   }
   pcp_stats_t& L = h->last;
@@ -821,8 +914,7 @@ int pcp_history_attention_workspace_size(const pcp_dims_t* dims, int64_t total_v
   PCP_TRY(check_dims(dims));
   if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
   const int ms = max_splits_for(*dims);
-  const SplitPlan plan = plan_splits(m_units(*dims), std::max<int64_t>(1, ceil_div(total_valid, pcp::kTileN)),
-                                     num_sms(), ms);
+  const SplitPlan plan = plan_splits(*dims, total_valid, num_sms(), ms, true);
   *bytes = ws_layout(*dims, total_valid, plan.splits).total;
   return PCP_OK;
 }
@@ -858,9 +950,10 @@ int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* pac
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
   PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  const bool direct = part.plan.splits == 1;
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
-  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
+  if (part.plan.splits > 1)
+    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
+                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
   return PCP_OK;
 }
 
@@ -869,7 +962,7 @@ int pcp_prefill_attention_workspace_size(const pcp_dims_t* dims, int64_t total_v
   if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
   int splits = 0;
   if (total_valid > 0)
-    splits = plan_splits(m_units(*dims), ceil_div(total_valid, pcp::kTileN), num_sms(), max_splits_for(*dims) - 1).splits;
+    splits = plan_splits(*dims, total_valid, num_sms(), max_splits_for(*dims) - 1, true).splits;
   *bytes = ws_layout(*dims, total_valid + current_keys(*dims), splits + 1).total;
   return PCP_OK;
 }
@@ -953,9 +1046,10 @@ int pcp_history_attention_paged(const pcp_dims_t* dims, const void* q, const voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
   PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  const bool direct = part.plan.splits == 1;
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
-  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
+  if (part.plan.splits > 1)
+    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
+                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
   return PCP_OK;
 }
 
@@ -1091,7 +1185,7 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
   int split_cap = max_splits_for(d);
   Workspace w;
   while (true) {
-    part.plan = plan_splits(m_units(d), n_kt, sms, split_cap);
+    part.plan = plan_splits(d, part.keys, sms, split_cap, true);
     w = ws_layout(d, part.keys, part.plan.splits);
     if (w.total <= PCP_NOALLOC_SCRATCH_BYTES) break;
     if (part.plan.splits == 1)
@@ -1110,9 +1204,10 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
   // map's extent) and every partial the combine reads is rewritten.
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
   PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  const bool direct = part.plan.splits == 1;
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, direct, out, st, nullptr));
-  if (!direct) PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr));
+  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
+  if (part.plan.splits > 1)
+    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
+                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
   CUDA_TRY(cudaMemcpyAsync(device_status, ws, sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
   return PCP_OK;
 }

@@ -51,7 +51,8 @@ def test_rank_matches_oracle(name, cfg, kv_dtype, ranks):
 
 
 def test_single_rank_handle_direct_output():
-    """P = 1 through the handle: many Q tiles, one split, bf16 written by TMA."""
+    """P = 1 through the handle: one stream-K attention launch writes every
+    unit one segment covers as bf16 output; the combine merges the rest."""
     cfg = PCPAttentionConfig(1, 1024, 4096, 4096, 512, 64, 32, 2, 256)
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=7)
     packed = packed_shards(cfg, k_shards, v_shards)[0].cuda()
@@ -59,7 +60,7 @@ def test_single_rank_handle_direct_output():
     out = attn(q_shards[0].cuda(), packed)
     attn.status()
     st = attn.stats()
-    assert st["splits"] == 1 and st["attn_launches"] == 1
+    assert st["attn_launches"] == 1 and st["kernel_launches"] <= 3  # unpack, attention, combine
     assert_parity(out, expected_rank_output(cfg, q, k, v, 0), "p1 direct")
     attn.close()
 
