@@ -92,6 +92,7 @@ SIGNATURES = {
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
     "pcp_device_status": (_c.c_int, [_P, _I32]),
     "pcp_set_exchange": (_c.c_int, [_P, _I32]),
+    "pcp_set_comm_sms": (_c.c_int, [_P, _I32]),
     "pcp_set_profiling": (_c.c_int, [_P, _I32]),
     "pcp_get_stats": (_c.c_int, [_P, _c.POINTER(PcpStats)]),
     "pcp_destroy": (_c.c_int, [_P]),

@@ -449,10 +449,17 @@ struct Part {
   int64_t keys = 0;
   SplitPlan plan;
   bool last = true;  // the forward's last history launch (no exchange in flight)
+  int sms = 0;       // SMs the launch may use (0: all); fewer leave SMs to an exchange in flight
 };
 
 int plan_part(const pcp_dims_t& d, Part* part, int sms, int max_splits) {
   if (part->keys == 0) return PCP_OK;
+  if (part->sms > 0 && part->sms < sms) {
+    // A launch that shares the GPU with an exchange: a persistent grid on
+    // part->sms SMs (stream-K; the caller checked that its K/V fits in L2).
+    part->plan = plan_stream_k(m_units(d), ceil_div(part->keys, pcp::kTileN), part->sms, max_splits);
+    return PCP_OK;
+  }
   part->plan = plan_splits(d, part->keys, sms, max_splits, part->last);
   return PCP_OK;
 }
@@ -501,6 +508,7 @@ struct pcp_handle {
   uint8_t* cur_k = nullptr;  // [P][Hkv][Qloc][D] bf16: current tokens' K of every rank (P > 1)
   uint8_t* cur_v = nullptr;
   int exchange = PCP_EXCHANGE_DIRECT;
+  int comm_sms = 16;  // SMs left to the direct exchange while the local shard is attended (P >= 4)
   uint8_t* ws = nullptr;
   Workspace w;
   // staging for pcp_forward_host
@@ -746,11 +754,23 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       // attended while the second group's travel; otherwise one group (fewer
       // launches and split partials).  Pairs match across ranks: at step s
       // rank r sends to r+s, which receives from (r+s)-s = r in the same group.
+      // With at least 4 ranks the exchange is long enough to matter.  If the
+      // local shard's K/V fits in L2, attend it on a persistent grid that
+      // leaves comm_sms SMs to NCCL, so all peers' shards travel in one group
+      // while it runs.  Otherwise, when the local wave-scheduled launch fills
+      // every SM pair (NCCL then only gets SMs between waves), exchange the
+      // peers in two groups and attend the first while the second travels.
+      const int64_t local_kv = static_cast<int64_t>(valid_len[r]) * d.num_kv_heads * d.head_dim * 4;
+      const bool reserve = P >= 4 && h->comm_sms > 0 && h->comm_sms < h->sms && parts[0].keys > 0 &&
+                           local_kv <= kStreamKMaxKvBytes;
+      if (reserve) parts[0].sms = h->sms - h->comm_sms;
       Part probe = parts[0];
       probe.last = false;
+      probe.sms = 0;
       plan_part(d, &probe, h->sms, max_splits);
-      const bool local_fills_gpu = probe.keys && probe.plan.pairs >= std::max(1, h->sms / 2);
-      const int groups = (P >= 4 && local_fills_gpu) ? 2 : 1;
+      const bool local_fills_gpu =
+          probe.keys && m_units(d) * probe.plan.splits >= std::max(1, h->sms / 2);
+      const int groups = (P >= 4 && !reserve && local_fills_gpu) ? 2 : 1;
       const int split_step = 1 + (P - 1 + 1) / 2;
       for (int g = 0; g < groups; ++g) {
         const int s0 = g == 0 ? 1 : split_step;
@@ -1380,6 +1400,13 @@ int pcp_set_exchange(pcp_handle_t* h, int32_t mode) {
   if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING && mode != PCP_EXCHANGE_ALLGATHER)
     return fail(PCP_ERR_INVALID_ARGUMENT, "exchange mode %d unknown", mode);
   h->exchange = mode;
+  return PCP_OK;
+}
+
+int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  if (sms < 0 || sms >= h->sms) return fail(PCP_ERR_INVALID_ARGUMENT, "comm_sms %d outside [0, %d)", sms, h->sms);
+  h->comm_sms = sms & ~1;  // whole SM pairs
   return PCP_OK;
 }
 

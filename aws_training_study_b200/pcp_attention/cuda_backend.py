@@ -115,6 +115,8 @@ class HistoryAttention:
     ``exchange`` picks how the shards reach every rank: ``"direct"`` (each
     rank sends its shard to every peer in one NCCL group; the default on
     NVSwitch) or ``"ring"`` (the reference's store-and-forward ring).
+    ``comm_sms`` (default 16) is how many SMs the local-shard launch leaves to
+    the direct exchange when ``pcp_size >= 4`` (``pcp_set_comm_sms``).
     """
 
     def __init__(
@@ -125,6 +127,7 @@ class HistoryAttention:
         device: int | torch.device | None = None,
         group=None,
         exchange: str = "direct",
+        comm_sms: int | None = None,
     ):
         self.config = config
         self.kv_dtype = kv_dtype
@@ -164,6 +167,8 @@ class HistoryAttention:
             raise ValueError(f"exchange must be one of {sorted(modes)}, got {exchange!r}")
         _capi.check(lib.pcp_set_exchange(self._handle, modes[exchange]))
         self.exchange = exchange
+        if comm_sms is not None:
+            _capi.check(lib.pcp_set_comm_sms(self._handle, int(comm_sms)))
 
     # -- calls -------------------------------------------------------------
     def _check_inputs(self, q: torch.Tensor, packed_kv: torch.Tensor) -> None:

@@ -266,7 +266,8 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
     q, packed = make_local_baseline_inputs(cfg, args.seed, rank, kv_dtype=kv_dtype, outlier_frac=wl["outliers"],
                                            device=dev)
     valid = cfg.source_valid_lens()
-    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank, exchange=args.exchange)
+    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank, exchange=args.exchange,
+                            comm_sms=args.comm_sms)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream()
     flops_step = 4.0 * cfg.num_q_heads * cfg.current_len * cfg.actual_history_len * cfg.head_dim
@@ -445,6 +446,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
+    ap.add_argument("--comm-sms", type=int, default=None,
+                    help="SMs the local-shard launch leaves to the exchange at 4+ ranks (library default 16)")
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")
     ap.add_argument("--history", type=int, default=None, help="override the workload's history length (profiling)")
     ap.add_argument("--e2e-steps", type=int, default=10)

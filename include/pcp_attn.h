@@ -284,6 +284,15 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms);
 enum pcp_exchange { PCP_EXCHANGE_DIRECT = 0, PCP_EXCHANGE_RING = 1, PCP_EXCHANGE_ALLGATHER = 2 };
 int pcp_set_exchange(pcp_handle_t* h, int32_t mode);
 
+/* SMs left to the direct exchange while the local shard is attended, with
+ * pcp_size >= 4 and a local shard whose dense bf16 K/V fits in L2: that
+ * launch then runs on a persistent grid of the other SMs and every peer's
+ * shard travels in one NCCL group meanwhile (NCCL's kernels need SMs; a
+ * launch on all of them would hold them off until it ends).  0 turns it off
+ * (the exchange then goes in two groups when the local launch fills the
+ * GPU).  Default 16; rounded down to whole SM pairs. */
+int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms);
+
 int pcp_set_profiling(pcp_handle_t* h, int32_t enable);
 int pcp_get_stats(const pcp_handle_t* h, pcp_stats_t* out);
 int pcp_destroy(pcp_handle_t* h);
