@@ -72,6 +72,8 @@ SIGNATURES = {
     "pcp_abi_version": (_c.c_int, []),
     "pcp_source_valid_len": (_c.c_int64, [_c.c_int64, _I32, _I32, _I32]),
     "pcp_ring_schedule": (_c.c_int, [_I32, _I32, _I32, _PI32, _PI32, _PI32, _PI32]),
+    "pcp_stream_k_plan": (_c.c_int, [_c.c_int64, _c.c_int64, _I32, _I32, _PI32, _PI32]),
+    "pcp_stream_k_segments": (_c.c_int, [_I32, _I32, _I32, _I32, _PI32, _I32, _PI32]),
     "pcp_nccl_unique_id_bytes": (_c.c_int, []),
     "pcp_get_nccl_unique_id": (_c.c_int, [_P]),
     "pcp_history_attention_workspace_size": (_c.c_int, [_PDIMS, _c.c_int64, _c.POINTER(_c.c_size_t)]),

@@ -52,18 +52,19 @@ struct PairSmemSK {
 struct Segment {
   int unit;
   int kt0, kt1;
-  int slot;  // partial slot within the unit (stream-K) or the split (static)
-  int nseg;  // segments the unit is cut into (stream-K; 1 in static mode)
-  bool last; // the segment ends the unit's key range (stream-K)
+  int slot;  // partial slot of this segment within its unit
+  int nseg;  // segments the unit is cut into
+  bool last; // the segment ends the unit's key range
 };
 
-// Stream-K segments of one CTA pair, identical in every role of both CTAs.
+// Stream-K segments of one CTA pair, identical in every role of both CTAs
+// (host-callable too: pcp_stream_k_segments exposes it for tests).
 struct Schedule {
   int n_kt, units;
   long long T, t, t_end;
   int pairs, g;
 
-  __device__ void init_stream_k(int n_kt_, int units_, int grid_pairs, int pair) {
+  __host__ __device__ void init_stream_k(int n_kt_, int units_, int grid_pairs, int pair) {
     n_kt = n_kt_;
     units = units_;
     T = static_cast<long long>(units) * n_kt;
@@ -79,14 +80,15 @@ struct Schedule {
     }
   }
   // First pair whose range holds tile x (ranges [T g / G, T (g + 1) / G)).
-  __device__ long long pair_of(long long x) const { return stream_k_pair_of(x, T, pairs); }
-  __device__ bool next(Segment& s) {
+  __host__ __device__ long long pair_of(long long x) const { return stream_k_pair_of(x, T, pairs); }
+  __host__ __device__ bool next(Segment& s) {
     if (t >= t_end) return false;
     const int u = static_cast<int>(t / n_kt);
     const long long ub = static_cast<long long>(u) * n_kt;
     s.unit = u;
     s.kt0 = static_cast<int>(t - ub);
-    s.kt1 = static_cast<int>(min(static_cast<long long>(n_kt), t_end - ub));
+    const long long end = t_end - ub;
+    s.kt1 = static_cast<int>(end < n_kt ? end : n_kt);
     const long long g0 = pair_of(ub);
     s.slot = static_cast<int>(g - g0);
     s.nseg = static_cast<int>(pair_of(ub + n_kt - 1) - g0 + 1);

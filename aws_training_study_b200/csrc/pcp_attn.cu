@@ -1403,6 +1403,41 @@ int pcp_set_exchange(pcp_handle_t* h, int32_t mode) {
   return PCP_OK;
 }
 
+int pcp_stream_k_plan(int64_t units, int64_t key_tiles, int32_t sms, int32_t slot_cap, int32_t* pairs,
+                      int32_t* slots) {
+  if (units <= 0 || key_tiles < 0 || sms <= 0 || slot_cap <= 0 || !pairs || !slots)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
+  const SplitPlan pl = plan_stream_k(units, key_tiles, sms, slot_cap);
+  *pairs = pl.pairs;
+  *slots = pl.splits;
+  return PCP_OK;
+}
+
+int pcp_stream_k_segments(int32_t units, int32_t key_tiles, int32_t grid_pairs, int32_t pair, int32_t* segments,
+                          int32_t max_segments, int32_t* count) {
+  if (units <= 0 || key_tiles < 0 || grid_pairs <= 0 || pair < 0 || pair >= grid_pairs || !count ||
+      (max_segments > 0 && !segments))
+    return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
+  pcp::Schedule sc;
+  sc.init_stream_k(key_tiles, units, grid_pairs, pair);
+  pcp::Segment sg;
+  int n = 0;
+  while (sc.next(sg)) {
+    if (n < max_segments) {
+      int32_t* o = segments + 6 * n;
+      o[0] = sg.unit;
+      o[1] = sg.kt0;
+      o[2] = sg.kt1;
+      o[3] = sg.slot;
+      o[4] = sg.nseg;
+      o[5] = sg.last ? 1 : 0;
+    }
+    ++n;
+  }
+  *count = n;
+  return n > max_segments ? fail(PCP_ERR_INVALID_ARGUMENT, "%d segments, room for %d", n, max_segments) : PCP_OK;
+}
+
 int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
   if (sms < 0 || sms >= h->sms) return fail(PCP_ERR_INVALID_ARGUMENT, "comm_sms %d outside [0, %d)", sms, h->sms);

@@ -107,6 +107,18 @@ int pcp_ring_schedule(int32_t rank, int32_t pcp_size, int32_t hop, int32_t* send
 int pcp_nccl_unique_id_bytes(void);
 int pcp_get_nccl_unique_id(void* out);
 
+/* Host-side view of the stream-K schedule of a history launch (the same
+ * arithmetic the kernel runs), for tests and tools.  pcp_stream_k_plan: the
+ * CTA pairs and partial slots per unit the planner picks for `units`
+ * 256-row units x `key_tiles` 128-key tiles on `sms` SMs within `slot_cap`
+ * slots.  pcp_stream_k_segments: the segments pair `pair` of a
+ * `grid_pairs` grid walks, 6 int32 each (unit, first tile, end tile, slot,
+ * segments of the unit, ends the unit); *count gets the number. */
+int pcp_stream_k_plan(int64_t units, int64_t key_tiles, int32_t sms, int32_t slot_cap, int32_t* pairs,
+                      int32_t* slots);
+int pcp_stream_k_segments(int32_t units, int32_t key_tiles, int32_t grid_pairs, int32_t pair, int32_t* segments,
+                          int32_t max_segments, int32_t* count);
+
 /* ---- stateless single-GPU entry ---------------------------------------- */
 
 /* Device workspace bytes needed by pcp_history_attention for `total_valid`
