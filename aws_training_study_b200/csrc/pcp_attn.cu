@@ -88,7 +88,8 @@ int make_tmap(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, u
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
 
-// Attention schedules (AttnParams::stream_k).
+// Attention schedules: the wave-scheduled kernel (attn_pair.cuh) or the
+// stream-K kernel (attn_pair_sk.cuh).
 constexpr int kModeStatic = 0;   // one (unit, key split) item per CTA pair, in waves
 constexpr int kModeStreamK = 1;  // equal contiguous (unit, tile) ranges per persistent pair
 // Stream-K only while the launch's bf16 K/V stays well inside the 126 MB L2
@@ -142,17 +143,6 @@ SplitPlan plan_static(int64_t units, int64_t n_kt, int sms, int slot_cap) {
   return best;
 }
 
-int64_t m_units_of(const pcp_dims_t& d);
-
-// The schedule of a history launch over `keys` dense keys (or their bound).
-// `last`: no exchange is in flight while it runs (the forward's last launch).
-SplitPlan plan_splits(const pcp_dims_t& d, int64_t keys, int sms, int slot_cap, bool last) {
-  const int64_t n_kt = std::max<int64_t>(1, ceil_div(keys, pcp::kTileN));
-  const int64_t kv_bytes = keys * d.num_kv_heads * d.head_dim * 4;
-  return last && kv_bytes <= kStreamKMaxKvBytes ? plan_stream_k(m_units_of(d), n_kt, sms, slot_cap)
-                                                : plan_static(m_units_of(d), n_kt, sms, slot_cap);
-}
-
 int check_dims(const pcp_dims_t* d) {
   if (!d) return fail(PCP_ERR_INVALID_ARGUMENT, "dims is NULL");
   if (d->pcp_size <= 0 || d->local_q_len <= 0 || d->max_local_blocks <= 0 || d->block_size <= 0 ||
@@ -191,7 +181,15 @@ int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q
 int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
 // Work units of one split: 256-row CTA-pair tiles over every KV head.
 int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kPairRows); }
-int64_t m_units_of(const pcp_dims_t& d) { return m_units(d); }
+// The schedule of a history launch over `keys` dense keys (or their bound).
+// `last`: no exchange is in flight while it runs (the forward's last launch).
+SplitPlan plan_splits(const pcp_dims_t& d, int64_t keys, int sms, int slot_cap, bool last) {
+  const int64_t n_kt = std::max<int64_t>(1, ceil_div(keys, pcp::kTileN));
+  const int64_t kv_bytes = keys * d.num_kv_heads * d.head_dim * 4;
+  return last && kv_bytes <= kStreamKMaxKvBytes ? plan_stream_k(m_units(d), n_kt, sms, slot_cap)
+                                                : plan_static(m_units(d), n_kt, sms, slot_cap);
+}
+
 
 int num_sms() {
   int dev = 0, sms = 148;
