@@ -447,12 +447,146 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def run_rows(args, wl, rank: int, world: int, local_rank: int) -> int:
+    """Measurements of the steps next to the history attention (one JSON line
+    each, rank 0; device time with CUDA events, max over ranks):
+      prefill     -- HistoryAttention.prefill: history plus causal attention
+                     over the current tokens of every rank; useful FLOPs are
+                     the history's plus the visible (query, current key) pairs;
+      cache-write -- the paged-cache producer writing one prefill's current
+                     tokens (bf16 in, cache dtype out) through a block table;
+      graph       -- one forward as a recorded length-bucket CUDA graph vs the
+                     eager call, host wall clock per call with a sync (the
+                     launch overhead a graph removes)."""
+    import torch
+    import torch.distributed as dist
+
+    from aws_training_study_b200.pcp_attention import PCPAttentionConfig
+    from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
+    from aws_training_study_b200.pcp_attention.graphs import BucketGraph, bucket_for
+    from aws_training_study_b200.pcp_attention.inputs import make_local_baseline_inputs
+    from aws_training_study_b200.pcp_attention.paged import cache_write, make_pool
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    kv_dtype = torch.float8_e4m3fn if wl["kv"] == "e4m3" else torch.bfloat16
+    cfg = PCPAttentionConfig(
+        pcp_size=world, current_len=wl["current_len"], max_history_len=wl["max_history_len"],
+        actual_history_len=wl["actual_history_len"], block_size=wl["block_size"],
+        interleave_size=wl["interleave_size"], num_q_heads=wl["num_q_heads"], num_kv_heads=wl["num_kv_heads"],
+        head_dim=wl["head_dim"],
+    ).validate()
+    q, packed = make_local_baseline_inputs(cfg, args.seed, rank, kv_dtype=kv_dtype, outlier_frac=wl["outliers"],
+                                           device=dev)
+    valid = cfg.source_valid_lens()
+    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank, exchange=args.exchange,
+                            comm_sms=args.comm_sms)
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 7919 + rank)
+    warm = max(3, args.warmup)
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def device_ms(fn) -> float:
+        for _ in range(warm):
+            fn()
+        attn.status(600000)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        attn.status(600000)
+        return max_over_ranks(t0.elapsed_time(t1) / args.steps)
+
+    line = None
+    hist_flops = 4.0 * cfg.num_q_heads * cfg.current_len * cfg.actual_history_len * cfg.head_dim
+    if args.mode == "prefill":
+        shape = (cfg.num_kv_heads, cfg.local_q_len, cfg.head_dim)
+        k_cur = (torch.randn(shape, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+        v_cur = (torch.randn(shape, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        ms = device_ms(lambda: attn.prefill(q, packed, k_cur, v_cur, valid, out))
+        hist_ms = device_ms(lambda: attn(q, packed, valid, out))
+        qlen = cfg.current_len
+        flops = hist_flops + 4.0 * cfg.num_q_heads * cfg.head_dim * qlen * (qlen + 1) / 2
+        line = {"metric": "prefill TFLOP/s (history + causal current tokens, useful FLOPs), device-timed max over ranks",
+                "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "history_only_ms": hist_ms, "causal_overhead_ms": ms - hist_ms, "higher_is_better": True}
+    elif args.mode == "cache-write":
+        nb = cfg.max_local_blocks
+        table = torch.randperm(nb + 8, generator=torch.Generator().manual_seed(rank), dtype=torch.int32)[:nb].to(dev)
+        pool = make_pool(cfg, nb + 8, kv_dtype, dev)
+        tokens = cfg.current_len
+        first = max(0, cfg.max_history_len - tokens)
+        shape = (cfg.num_kv_heads, tokens, cfg.head_dim)
+        k_new = (torch.randn(shape, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+        v_new = (torch.randn(shape, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        ms = device_ms(lambda: cache_write(cfg, rank, first, k_new, v_new, table, pool, status))
+        if int(status.item()) != 0:
+            raise RuntimeError(f"cache_write reported {int(status.item())}")
+        owned = tokens // world  # the stripe gives every rank the same share of an aligned range
+        elt = 1 if kv_dtype == torch.float8_e4m3fn else 2
+        moved = 2 * cfg.num_kv_heads * owned * cfg.head_dim * (2 + elt) * world
+        line = {"metric": "paged-cache write GB/s (bf16 in, cache dtype out, all ranks), device-timed max over ranks",
+                "value": moved / (ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "tokens": tokens,
+                "higher_is_better": True}
+    else:  # graph
+        out = torch.empty_like(q)
+        bucket = bucket_for(cfg, valid)
+        g = BucketGraph(attn, bucket, q, packed, out)
+
+        def host_us(fn) -> float:
+            for _ in range(warm):
+                fn()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            times = []
+            for _ in range(args.steps):
+                t = time.perf_counter()
+                fn()
+                torch.cuda.synchronize()
+                times.append((time.perf_counter() - t) * 1e6)
+            return max_over_ranks(statistics.median(times))
+
+        eager_us = host_us(lambda: attn(q, packed, valid, out))
+        graph_us = host_us(lambda: g.replay(valid))
+        attn.status(600000)
+        line = {"metric": "forward latency us (bucketed CUDA graph replay), host wall clock per call with sync, "
+                          "median, max over ranks",
+                "value": graph_us, "unit": "us", "eager_us": eager_us, "bucket": list(bucket),
+                "higher_is_better": False}
+    if rank == 0:
+        line.update({"mode": args.mode, "n_gpus": world, "steps": args.steps, "warmup": warm, "dtype": "bf16",
+                     "data": "synthetic", "config": {"workload": wl["desc"], "pcp_size": world}})
+        print(json.dumps(line), flush=True)
+    attn.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--mode", choices=("history", "prefill", "cache-write", "graph"), default="history",
+                    help="history (the headline metric) or a measurement of a neighbouring step")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
@@ -484,6 +618,8 @@ def main() -> int:
         wl["desc"] += f" [override: history={args.history}]"
     if args.impl == "reference":
         return run_reference(args, wl, rank, world)
+    if args.mode != "history":
+        return run_rows(args, wl, rank, world, local_rank)
     return run_ours(args, wl, rank, world, local_rank)
 
 
