@@ -745,19 +745,17 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       // Direct exchange over NVSwitch: each rank sends its own shard to every
       // peer and receives every peer's shard straight from its owner -- the
       // same bytes per rank as the ring, no forwarding chain, and no shard
-      // returns to its owner.  When the local-shard launch fills every SM
-      // pair (so NCCL's kernels only get SMs as it drains) and there are at
-      // least 4 ranks, the peers are exchanged in two NCCL groups (ring steps
-      // 1..ceil((P-1)/2), then the rest) and the first group's shards are
-      // attended while the second group's travel; otherwise one group (fewer
-      // launches and split partials).  Pairs match across ranks: at step s
-      // rank r sends to r+s, which receives from (r+s)-s = r in the same group.
-      // With at least 4 ranks the exchange is long enough to matter.  If the
-      // local shard's K/V fits in L2, attend it on a persistent grid that
-      // leaves comm_sms SMs to NCCL, so all peers' shards travel in one group
-      // while it runs.  Otherwise, when the local wave-scheduled launch fills
-      // every SM pair (NCCL then only gets SMs between waves), exchange the
-      // peers in two groups and attend the first while the second travels.
+      // returns to its owner.  Pairs match across ranks: at step s rank r
+      // sends to r+s, which receives from (r+s)-s = r in the same group.
+      // With at least 4 ranks the exchange is long enough to matter, and
+      // NCCL's kernels need SMs while the local shard is attended:
+      //   * local K/V fits in L2: attend it on a persistent grid that leaves
+      //     comm_sms SMs to NCCL; all peers travel in one group meanwhile;
+      //   * else, when the local wave-scheduled launch fills every SM pair
+      //     (NCCL then only gets SMs between waves): two groups (ring steps
+      //     1..ceil((P-1)/2), then the rest), the first group's shards
+      //     attended while the second group's travel;
+      //   * else one group (fewer launches and split partials).
       const int64_t local_kv = static_cast<int64_t>(valid_len[r]) * d.num_kv_heads * d.head_dim * 4;
       const bool reserve = P >= 4 && h->comm_sms > 0 && h->comm_sms < h->sms && parts[0].keys > 0 &&
                            local_kv <= kStreamKMaxKvBytes;
@@ -810,8 +808,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       if (part.keys && (!big || part.plan.splits > big->plan.splits)) big = &part;
     if (!big || big->plan.splits == 1) return fail(PCP_ERR_UNSUPPORTED, "too many launches for the partial buffers");
     const int others = total_splits - big->plan.splits;
-    big->plan = plan_splits(d, big->keys, h->sms, std::max(1, std::min(big->plan.splits - 1, hist_cap - others)),
-                            big->last);
+    plan_part(d, big, h->sms, std::max(1, std::min(big->plan.splits - 1, hist_cap - others)));
     total_splits = others + big->plan.splits;
   }
   if (with_cur) ++total_splits;
