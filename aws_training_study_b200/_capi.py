@@ -18,6 +18,7 @@ PCP_KV_BF16 = 1
 PCP_EXCHANGE_DIRECT = 0
 PCP_EXCHANGE_RING = 1
 PCP_EXCHANGE_ALLGATHER = 2
+PCP_EXCHANGE_PIPELINE = 3
 
 STATUS_NAMES = {
     0: "PCP_OK",

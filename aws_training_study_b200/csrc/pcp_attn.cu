@@ -500,6 +500,7 @@ struct pcp_handle {
   cudaStream_t last_stream = nullptr;
   cudaEvent_t ev_in = nullptr, ev_comm = nullptr;
   cudaEvent_t ev_group[2] = {nullptr, nullptr};  // direct exchange: shards of each peer group landed
+  std::vector<cudaEvent_t> ev_step;              // pipelined exchange: shards of each step chunk landed
   cudaEvent_t ev_cur = nullptr;                  // current tokens' K/V of every rank landed
   uint8_t* ring = nullptr;  // [P][max_local_blocks][payload]: slot s receives source s
   uint8_t* stage = nullptr;  // [max_local_blocks][payload]: a paged shard's blocks gathered for sending
@@ -741,6 +742,27 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       }
       CUDA_TRY(cudaEventRecord(h->ev_comm, h->comm_stream));
       add_part(1, P, h->ev_comm);
+    } else if (h->exchange == PCP_EXCHANGE_PIPELINE) {
+      // Direct sends and receives, one NCCL group per chunk of ring steps
+      // (one step per chunk up to kMaxParts - 1 chunks): each chunk's shards
+      // are attended as soon as they land while the later chunks travel.
+      const int chunks = std::min<int>(P - 1, static_cast<int>(h->ev_step.size()));
+      for (int k = 0; k < chunks; ++k) {
+        const int s0 = 1 + (P - 1) * k / chunks;
+        const int s1 = 1 + (P - 1) * (k + 1) / chunks;
+        ncclResult_t nr = ncclGroupStart();
+        if (nr != ncclSuccess) return fail(PCP_ERR_NCCL, "ncclGroupStart: %s", ncclGetErrorString(nr));
+        for (int step = s0; step < s1; ++step) {
+          const int to = (r + step) % P;
+          const int from = ((r - step) % P + P) % P;
+          if (live(r)) ncclSend(own, live(r), ncclUint8, to, h->comm, h->comm_stream);
+          if (live(from)) ncclRecv(slot(from), live(from), ncclUint8, from, h->comm, h->comm_stream);
+          sent += static_cast<int64_t>(live(r));
+        }
+        PCP_TRY(wait_nccl(h->comm, ncclGroupEnd(), 600000));
+        CUDA_TRY(cudaEventRecord(h->ev_step[k], h->comm_stream));
+        add_part(s0, s1, h->ev_step[k]);
+      }
     } else {
       // Direct exchange over NVSwitch: each rank sends its own shard to every
       // peer and receives every peer's shard straight from its owner -- the
@@ -797,6 +819,14 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     if (parts[i].keys) last_live = static_cast<int>(i);
   }
   if (last_live >= 0) parts[last_live].last = true;
+  // Pipelined exchange: every launch but the last shares the GPU with chunks
+  // still in flight -- on a persistent grid that leaves comm_sms SMs to NCCL
+  // where its K/V fits in L2.
+  if (P > 1 && h->exchange == PCP_EXCHANGE_PIPELINE && h->comm_sms > 0 && h->comm_sms < h->sms)
+    for (auto& part : parts)
+      if (part.keys && !part.last &&
+          part.keys * d.num_kv_heads * d.head_dim * 4 <= kStreamKMaxKvBytes)
+        part.sms = h->sms - h->comm_sms;
   int total_splits = 0;
   for (auto& part : parts) {
     plan_part(d, &part, h->sms, hist_cap);
@@ -1271,6 +1301,10 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
         cudaEventCreateWithFlags(&h->ev_group[1], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&h->ev_cur, cudaEventDisableTiming) != cudaSuccess)
       return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
+    h->ev_step.assign(std::min(d.pcp_size - 1, kMaxParts - 1), nullptr);
+    for (auto& e : h->ev_step)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+        return cleanup(fail(PCP_ERR_CUDA, "event creation failed"));
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
@@ -1392,7 +1426,8 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms) {
 
 int pcp_set_exchange(pcp_handle_t* h, int32_t mode) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
-  if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING && mode != PCP_EXCHANGE_ALLGATHER)
+  if (mode != PCP_EXCHANGE_DIRECT && mode != PCP_EXCHANGE_RING && mode != PCP_EXCHANGE_ALLGATHER &&
+      mode != PCP_EXCHANGE_PIPELINE)
     return fail(PCP_ERR_INVALID_ARGUMENT, "exchange mode %d unknown", mode);
   h->exchange = mode;
   return PCP_OK;
@@ -1498,6 +1533,8 @@ int pcp_destroy(pcp_handle_t* h) {
   if (h->ev_in) cudaEventDestroy(h->ev_in);
   if (h->ev_comm) cudaEventDestroy(h->ev_comm);
   for (auto& e : h->ev_group)
+    if (e) cudaEventDestroy(e);
+  for (auto& e : h->ev_step)
     if (e) cudaEventDestroy(e);
   if (h->ev_cur) cudaEventDestroy(h->ev_cur);
   if (h->comm_stream) cudaStreamDestroy(h->comm_stream);

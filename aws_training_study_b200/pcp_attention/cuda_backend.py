@@ -114,7 +114,9 @@ class HistoryAttention:
 
     ``exchange`` picks how the shards reach every rank: ``"direct"`` (each
     rank sends its shard to every peer in one NCCL group; the default on
-    NVSwitch) or ``"ring"`` (the reference's store-and-forward ring).
+    NVSwitch), ``"ring"`` (the reference's store-and-forward ring),
+    ``"allgather"`` (one NCCL all-gather) or ``"pipeline"`` (one group per
+    ring step, each step's shard attended as soon as it lands).
     ``comm_sms`` (default 16) is how many SMs the local-shard launch leaves to
     the direct exchange when ``pcp_size >= 4`` (``pcp_set_comm_sms``).
     """
@@ -161,7 +163,7 @@ class HistoryAttention:
             _capi.check(lib.pcp_create(ctypes.byref(self._dims), self.rank, self.device.index, uid, ctypes.byref(handle)))
         self._handle = handle
         modes = {"direct": _capi.PCP_EXCHANGE_DIRECT, "ring": _capi.PCP_EXCHANGE_RING,
-                 "allgather": _capi.PCP_EXCHANGE_ALLGATHER}
+                 "allgather": _capi.PCP_EXCHANGE_ALLGATHER, "pipeline": _capi.PCP_EXCHANGE_PIPELINE}
         if exchange not in modes:
             self.close()
             raise ValueError(f"exchange must be one of {sorted(modes)}, got {exchange!r}")

@@ -589,7 +589,7 @@ def main() -> int:
                     help="history (the headline metric) or a measurement of a neighbouring step")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
+    ap.add_argument("--exchange", choices=("direct", "ring", "allgather", "pipeline"), default="direct")
     ap.add_argument("--comm-sms", type=int, default=None,
                     help="SMs the local-shard launch leaves to the exchange at 4+ ranks (library default 16)")
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")

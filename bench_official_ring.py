@@ -42,7 +42,7 @@ def parse_args() -> argparse.Namespace:
     parser.add_argument("--warmups", type=int, default=3)
     parser.add_argument("--iterations", type=int, default=20)
     parser.add_argument("--seed", type=int, default=20260907)
-    parser.add_argument("--exchange", choices=("direct", "ring", "allgather"), default="direct")
+    parser.add_argument("--exchange", choices=("direct", "ring", "allgather", "pipeline"), default="direct")
     parser.add_argument("--phases", action="store_true",
                         help="after timing, profile a few calls and print rank 0's per-phase device time")
     return parser.parse_args()

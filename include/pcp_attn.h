@@ -291,9 +291,18 @@ int pcp_device_status(pcp_handle_t* h, int32_t timeout_ms);
  *     owner (NVSwitch gives every pair full bandwidth);
  *   PCP_EXCHANGE_RING -- the reference's store-and-forward ring
  *     (kernel.py:276-293): P-1 hops to rank+1, schedule of pcp_ring_schedule;
+ *   PCP_EXCHANGE_PIPELINE -- direct sends, one NCCL group per ring step (up
+ *     to 7 groups), each step's shard attended as soon as it lands; every
+ *     launch but the last leaves pcp_set_comm_sms SMs to the exchange (for
+ *     exchanges that take as long as the compute, e.g. bf16 MHA shapes);
  *   PCP_EXCHANGE_ALLGATHER -- one NCCL all-gather of equal slots sized to the
  *     longest live shard (lets NCCL multicast through the switch). */
-enum pcp_exchange { PCP_EXCHANGE_DIRECT = 0, PCP_EXCHANGE_RING = 1, PCP_EXCHANGE_ALLGATHER = 2 };
+enum pcp_exchange {
+  PCP_EXCHANGE_DIRECT = 0,
+  PCP_EXCHANGE_RING = 1,
+  PCP_EXCHANGE_ALLGATHER = 2,
+  PCP_EXCHANGE_PIPELINE = 3
+};
 int pcp_set_exchange(pcp_handle_t* h, int32_t mode);
 
 /* SMs left to the direct exchange while the local shard is attended, with

@@ -60,6 +60,10 @@ def ring_ragged_allgather(rank, world):
     return _ring_body(rank, world, "ragged_d128_bf16", exchange="allgather")
 
 
+def ring_qwen_pipeline(rank, world):
+    return _ring_body(rank, world, "qwen_d256_fp8", exchange="pipeline")
+
+
 def prefill_ragged(rank, world):
     """History plus causal current tokens through the handle: the current
     K/V shards are all-gathered inside the C ABI."""
@@ -173,7 +177,7 @@ def ring_graph(rank, world):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather",
-                                "prefill_ragged", "ring_paged", "ring_graph"])
+                                "prefill_ragged", "ring_paged", "ring_graph", "ring_qwen_pipeline"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res
