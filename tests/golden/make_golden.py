@@ -1,6 +1,6 @@
 """Generate the golden fixtures in this folder by running the REFERENCE itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of HandsomeHow/aws_training_study>
 
 Imports the reference's own ``pcp_attention`` package and ``run_poc.py``
 (pure Python/torch, runnable on a CPU) and records their outputs on seeded
@@ -52,7 +52,7 @@ def randn_inputs(cfg, seed, scale=1.0):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of a checkout of the reference repository")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from pcp_attention.config import PCPAttentionConfig, get_preset
