@@ -44,7 +44,10 @@ class BucketGraph:
 
     ``replay(valid_len)`` writes the lengths into the graph's device buffer
     (an asynchronous copy on the current stream, ordered before the replay)
-    and launches the graph; the result lands in ``out``."""
+    and launches the graph on the current stream; the result lands in
+    ``out``.  ``HistoryAttention.status()`` watches the streams of its own
+    calls, not replays: synchronise the replay's stream (or consume ``out``
+    on it) before calling it to read a replay's device status."""
 
     def __init__(self, attn, bucket_len, q: torch.Tensor, packed_kv: torch.Tensor, out: torch.Tensor | None = None,
                  warmup: int = 1):
