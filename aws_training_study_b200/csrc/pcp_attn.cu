@@ -181,13 +181,28 @@ int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q
 int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
 // Work units of one split: 256-row CTA-pair tiles over every KV head.
 int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kPairRows); }
+// Relative cost of a plan in key tiles per SM pair: stream-K walks
+// ceil(steps / pairs) tiles plus ~2 tiles of prologue and partial write;
+// static runs waves of (tiles per item + 2).
+double plan_cost(const SplitPlan& pl, int64_t units, int64_t n_kt, int sms) {
+  if (pl.mode == kModeStreamK)
+    return static_cast<double>(ceil_div(units * n_kt, std::max(1, pl.pairs))) + 2.0;
+  const int64_t waves = ceil_div(units * pl.splits, std::max(1, sms / 2));
+  return static_cast<double>(waves) * (pl.tiles_per_split + 2.0);
+}
+
 // The schedule of a history launch over `keys` dense keys (or their bound).
 // `last`: no exchange is in flight while it runs (the forward's last launch).
+// Stream-K is kept only when the partial-slot cap leaves it a grid at least
+// as fast as the static schedule's (a cap of one or two slots can shrink the
+// stream-K grid to a few pairs).
 SplitPlan plan_splits(const pcp_dims_t& d, int64_t keys, int sms, int slot_cap, bool last) {
   const int64_t n_kt = std::max<int64_t>(1, ceil_div(keys, pcp::kTileN));
   const int64_t kv_bytes = keys * d.num_kv_heads * d.head_dim * 4;
-  return last && kv_bytes <= kStreamKMaxKvBytes ? plan_stream_k(m_units(d), n_kt, sms, slot_cap)
-                                                : plan_static(m_units(d), n_kt, sms, slot_cap);
+  const SplitPlan st = plan_static(m_units(d), n_kt, sms, slot_cap);
+  if (!last || kv_bytes > kStreamKMaxKvBytes) return st;
+  const SplitPlan sk = plan_stream_k(m_units(d), n_kt, sms, slot_cap);
+  return plan_cost(sk, m_units(d), n_kt, sms) <= plan_cost(st, m_units(d), n_kt, sms) ? sk : st;
 }
 
 
@@ -1224,9 +1239,10 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
     part.keys += valid_len[s];
   }
   if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
-  // The largest split plan whose workspace fits the fixed scratch.
+  // The largest split plan whose workspace fits the fixed scratch (a cap
+  // that starves stream-K of pairs falls back to the static schedule inside
+  // plan_splits).
   const int sms = num_sms();
-  const int64_t n_kt = ceil_div(part.keys, pcp::kTileN);
   int split_cap = max_splits_for(d);
   Workspace w;
   while (true) {

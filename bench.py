@@ -360,6 +360,10 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
             "api": "HistoryAttention.forward_host -> pcp_forward_host (C ABI), pinned host buffers",
         }
 
+    parity = None
+    if not args.no_parity:
+        parity = full_parity(cfg, args, wl, rank, world, dev, q, packed, out, valid, kv_dtype)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, dt, rows, desc = cpu_oracle_sample(wl, args.cpu_seconds)
@@ -417,11 +421,11 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
                           "TMEM accumulators), all attention launches of a step",
                 "bound": "tensor",
                 "achieved": achieved,
-                "peak": peaks["bf16_sustained"],
-                "peak_kind": f"bf16 dense, sustained ({peaks['source']})",
+                "peak": peaks["bf16"],
+                "peak_kind": f"bf16 dense, burst cuBLAS ({peaks['source']}): the timed region is under a second",
                 "unit": "TFLOP/s",
-                "frac": (achieved / peaks["bf16_sustained"]) if achieved else None,
-                "frac_of_burst": (achieved / peaks["bf16"]) if achieved else None,
+                "frac": (achieved / peaks["bf16"]) if achieved else None,
+                "frac_of_sustained": (achieved / peaks["bf16_sustained"]) if achieved else None,
                 "traffic": traffic,
                 "launches_timed": st["attn_launches"],
                 "avg_launch_ms": attn_ms_avg,
@@ -439,12 +443,59 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
                 "splits": st["splits"],
             },
         }
+        line["parity"] = parity
         print(json.dumps(line), flush=True)
     attn.close()
     if world > 1:
         barrier()
         dist.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        print(f"bench: output outside the parity bounds: {parity}", file=sys.stderr, flush=True)
+        return 3
     return 0
+
+
+def full_parity(cfg, args, wl, rank: int, world: int, dev, q, packed, out, valid, kv_dtype) -> dict:
+    """Every row of this rank's last timed output against the reference's
+    dense attention (reference.py:16-32) restated in torch fp32 on the GPU
+    (TF32 off, chunked over rows), over the whole history: the other ranks'
+    shards are regenerated here from their seeds.  Outside the timed region.
+    Returns the worst metrics over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from aws_training_study_b200.pcp_attention.check import (MAX_ABS, MEAN_ABS, MIN_NORM_RATIO, REL_L2, compare,
+                                                           dense_reference, history_from_packed)
+    from aws_training_study_b200.pcp_attention.inputs import make_local_baseline_inputs
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    shards = []
+    for s in range(world):
+        if s == rank:
+            shards.append(packed)
+        else:
+            shards.append(make_local_baseline_inputs(cfg, args.seed, s, kv_dtype=kv_dtype,
+                                                     outlier_frac=wl["outliers"], device=dev)[1])
+    k, v = history_from_packed(cfg, shards, valid)
+    del shards
+    ref = dense_reference(q, k, v, cfg.softmax_scale)
+    m = compare(out, ref)
+    del k, v, ref
+    worst = torch.tensor([m["max_abs"], m["mean_abs"], m["rel_l2"], -m["norm_ratio"], 0.0 if m["finite"] else 1.0],
+                         dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    w = worst.tolist()
+    res = {"max_abs": w[0], "mean_abs": w[1], "rel_l2": w[2], "norm_ratio_min": -w[3], "finite": w[4] == 0.0,
+           "ranks_checked": world, "rows_checked_per_rank": cfg.num_q_heads * cfg.local_q_len,
+           "reference": "dense fp32 attention over the whole history (reference.py:16-32 restated in torch, "
+                        "TF32 off), every output row of every rank, worst over ranks",
+           "bounds": {"max_abs": MAX_ABS, "mean_abs": MEAN_ABS, "rel_l2": REL_L2, "norm_ratio_min": MIN_NORM_RATIO},
+           "seconds": time.perf_counter() - t0}
+    res["ok"] = bool(res["finite"] and res["max_abs"] <= MAX_ABS and res["mean_abs"] <= MEAN_ABS
+                     and res["rel_l2"] <= REL_L2 and res["norm_ratio_min"] >= MIN_NORM_RATIO)
+    return res
 
 
 def run_rows(args, wl, rank: int, world: int, local_rank: int) -> int:
@@ -597,6 +648,7 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the full-output check after the timed steps")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
     args = ap.parse_args()
@@ -617,6 +669,12 @@ def main() -> int:
         wl["actual_history_len"] = wl["max_history_len"] = args.history
         wl["desc"] += f" [override: history={args.history}]"
     if args.impl == "reference":
+        # The CPU model uses every host core the process may run on, also under
+        # torchrun (which sets OMP_NUM_THREADS=1 for multi-rank jobs); numpy's
+        # BLAS reads these when the oracle first imports it.
+        threads = str(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1)
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = threads
         return run_reference(args, wl, rank, world)
     if args.mode != "history":
         return run_rows(args, wl, rank, world, local_rank)
