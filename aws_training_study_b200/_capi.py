@@ -19,6 +19,10 @@ PCP_EXCHANGE_DIRECT = 0
 PCP_EXCHANGE_RING = 1
 PCP_EXCHANGE_ALLGATHER = 2
 PCP_EXCHANGE_PIPELINE = 3
+PCP_KV_PATH_AUTO = 0
+PCP_KV_PATH_DENSE = 1
+PCP_KV_PATH_IN_PLACE = 2
+KV_PATHS = {"auto": PCP_KV_PATH_AUTO, "dense": PCP_KV_PATH_DENSE, "in_place": PCP_KV_PATH_IN_PLACE}
 
 STATUS_NAMES = {
     0: "PCP_OK",
@@ -63,6 +67,8 @@ class PcpStats(ctypes.Structure):
         ("forwards", _I32),
         ("ring_bytes", _c.c_int64),
         ("keys", _c.c_int64),
+        ("kv_in_place", _I32),
+        ("reserved", _I32),
     ]
 
 
@@ -96,6 +102,7 @@ SIGNATURES = {
     "pcp_device_status": (_c.c_int, [_P, _I32]),
     "pcp_set_exchange": (_c.c_int, [_P, _I32]),
     "pcp_set_comm_sms": (_c.c_int, [_P, _I32]),
+    "pcp_set_kv_path": (_c.c_int, [_P, _I32]),
     "pcp_set_profiling": (_c.c_int, [_P, _I32]),
     "pcp_get_stats": (_c.c_int, [_P, _c.POINTER(PcpStats)]),
     "pcp_destroy": (_c.c_int, [_P]),
@@ -138,3 +145,12 @@ def check(status: int) -> None:
 def int32_array(values) -> ctypes.Array:
     vals = [int(v) for v in values]
     return (ctypes.c_int32 * len(vals))(*vals)
+
+
+def set_default_kv_path(mode: str) -> None:
+    """Process default of how history launches read the KV cache
+    (``pcp_set_kv_path(NULL, ...)``): ``"auto"``, ``"dense"`` or ``"in_place"``."""
+    if mode not in KV_PATHS:
+        raise ValueError(f"kv path must be one of {sorted(KV_PATHS)}, got {mode!r}")
+    check(lib().pcp_set_kv_path(None, KV_PATHS[mode]))
+

@@ -291,8 +291,12 @@ struct CombineParams {
   // unit that one segment covered as final output; those rows are skipped.
   int skip_single;
   int units, grid_pairs, rows_per_head, m_tiles;
-  int num_keys;              // key count of the launch (or its bound)
-  const int* num_keys_dev;   // device-length mode: the actual count
+  // The launch's key tiles: `count` (or its bound), `count_dev` the actual
+  // number in device-length mode; both count keys (ceil(keys / 128) tiles)
+  // when count_is_keys (dense launches), else tiles (in-place launches).
+  int count;
+  const int* count_dev;
+  int count_is_keys;
 };
 
 template <int D>
@@ -301,8 +305,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int lane = threadIdx.x & 31;
   long long n_kt = 0, steps = 0, pairs = 1;
   if (p.skip_single) {
-    const int keys = p.num_keys_dev ? min(max(*p.num_keys_dev, 0), p.num_keys) : p.num_keys;
-    n_kt = (keys + kTileN - 1) / kTileN;
+    const int cnt = p.count_dev ? min(max(*p.count_dev, 0), p.count) : p.count;
+    n_kt = p.count_is_keys ? (cnt + kTileN - 1) / kTileN : cnt;
     steps = static_cast<long long>(p.units) * n_kt;
     pairs = stream_k_pairs(steps, p.grid_pairs);
   }

@@ -15,12 +15,14 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <thread>
 #include <vector>
 
 #include "attn_pair.cuh"
 #include "attn_pair_sk.cuh"
+#include "attn_kv.cuh"
 #include "kv_stage.cuh"
 
 namespace {
@@ -84,6 +86,25 @@ int make_tmap(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, u
   return PCP_OK;
 }
 
+// e4m3 cache blocks [blocks][2][Hkv][bs][D] (the packed payload), as a 5-D
+// byte tensor {D, bs, Hkv, K/V, blocks}; boxes of `box_x` bytes x 64 rows of
+// one head of K or V of one block, no swizzle.
+int make_tmap_blocks(CUtensorMap* tm, const void* base, const pcp_dims_t& d, int64_t blocks, uint32_t box_x) {
+  auto fn = encode_fn();
+  if (!fn) return fail(PCP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(PCP_ERR_INVALID_ARGUMENT, "KV cache not 16-byte aligned");
+  const uint64_t D = d.head_dim, bs = d.block_size, H = d.num_kv_heads;
+  cuuint64_t dims[5] = {D, bs, H, 2, static_cast<cuuint64_t>(std::max<int64_t>(blocks, 1))};
+  cuuint64_t strides[4] = {D, bs * D, H * bs * D, 2 * H * bs * D};
+  cuuint32_t box[5] = {box_x, 64, 1, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PCP_ERR_CUDA, "cuTensorMapEncodeTiled (cache blocks) failed (%d)", static_cast<int>(r));
+  return PCP_OK;
+}
+
 // --------------------------------------------------------------- planning --
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
@@ -95,6 +116,32 @@ constexpr int kModeStreamK = 1;  // equal contiguous (unit, tile) ranges per per
 // Stream-K only while the launch's bf16 K/V stays well inside the 126 MB L2
 // (its pairs read K/V at unrelated offsets).
 constexpr int64_t kStreamKMaxKvBytes = int64_t(48) << 20;
+
+// How a history launch reads the KV cache:
+//   * dense: kv_unpack_kernel expands the valid tokens into a dense bf16
+//     workspace once per forward, and attn_fwd_pair(_sk)_kernel reads it;
+//   * in place (e4m3 caches whose 64-key boxes never cross a cache block):
+//     attn_fwd_kv_kernel loads the cache blocks with TMA and upcasts them to
+//     f16 in shared memory -- no extra pass and no dense copy, but every
+//     256-row query unit converts every key tile again.
+// Measured at BASELINE configs[3] on one B200 (attention launch, TFLOP/s):
+// dense 1466 (+ a 0.1 ms unpack), in place 1296, in place with the
+// conversion skipped 1572.  The conversion therefore pays only while a
+// KV head has few query units: `auto` reads in place up to
+// kInPlaceMaxRows query rows per KV head.
+constexpr int64_t kInPlaceMaxRows = 1024;
+std::atomic<int> g_kv_path{PCP_KV_PATH_AUTO};  // process default (pcp_set_kv_path(NULL, ...))
+
+bool kv_in_place_ok(const pcp_dims_t& d) { return d.kv_dtype == PCP_KV_E4M3 && d.block_size % 64 == 0; }
+int64_t rows_per_head(const pcp_dims_t& d);
+bool choose_in_place(const pcp_dims_t& d, int mode) {
+  if (!kv_in_place_ok(d) || mode == PCP_KV_PATH_DENSE) return false;
+  return mode == PCP_KV_PATH_IN_PLACE || rows_per_head(d) <= kInPlaceMaxRows;
+}
+// Bytes of K and V one launch over `keys` keys reads: its L2 working set.
+int64_t kv_bytes(const pcp_dims_t& d, int64_t keys, bool in_place) {
+  return keys * d.num_kv_heads * d.head_dim * (in_place ? 2 : 4);
+}
 
 struct SplitPlan {
   int splits = 1;           // partial slots per unit the launch may write
@@ -191,18 +238,31 @@ double plan_cost(const SplitPlan& pl, int64_t units, int64_t n_kt, int sms) {
   return static_cast<double>(waves) * (pl.tiles_per_split + 2.0);
 }
 
-// The schedule of a history launch over `keys` dense keys (or their bound).
-// `last`: no exchange is in flight while it runs (the forward's last launch).
-// Stream-K is kept only when the partial-slot cap leaves it a grid at least
-// as fast as the static schedule's (a cap of one or two slots can shrink the
-// stream-K grid to a few pairs).
-SplitPlan plan_splits(const pcp_dims_t& d, int64_t keys, int sms, int slot_cap, bool last) {
-  const int64_t n_kt = std::max<int64_t>(1, ceil_div(keys, pcp::kTileN));
-  const int64_t kv_bytes = keys * d.num_kv_heads * d.head_dim * 4;
+// The schedule of a history launch over `tiles` key tiles (or their bound)
+// of `keys` keys.  `last`: no exchange is in flight while it runs (the
+// forward's last launch).  Stream-K is kept only when the partial-slot cap
+// leaves it a grid at least as fast as the static schedule's (a cap of one
+// or two slots can shrink the stream-K grid to a few pairs).
+SplitPlan plan_splits(const pcp_dims_t& d, int64_t tiles, int64_t keys, int sms, int slot_cap, bool last,
+                      bool in_place) {
+  const int64_t n_kt = std::max<int64_t>(1, tiles);
   const SplitPlan st = plan_static(m_units(d), n_kt, sms, slot_cap);
-  if (!last || kv_bytes > kStreamKMaxKvBytes) return st;
+  if (!last || kv_bytes(d, keys, in_place) > kStreamKMaxKvBytes) return st;
   const SplitPlan sk = plan_stream_k(m_units(d), n_kt, sms, slot_cap);
   return plan_cost(sk, m_units(d), n_kt, sms) <= plan_cost(st, m_units(d), n_kt, sms) ? sk : st;
+}
+
+// A plan made for `planned` tiles run over `actual` >= planned tiles (in
+// place, each source's last tile may be partial): the static schedule keeps
+// at most its split count and covers every tile; a stream-K grid covers any
+// tile count and never needs more slots than planned.
+SplitPlan fit_plan(SplitPlan pl, int64_t actual) {
+  if (pl.mode == kModeStatic) {
+    const int64_t n = std::max<int64_t>(1, actual);
+    pl.tiles_per_split = static_cast<int>(ceil_div(n, pl.splits));
+    pl.splits = static_cast<int>(ceil_div(n, pl.tiles_per_split));
+  }
+  return pl;
 }
 
 
@@ -426,9 +486,11 @@ SplitPlan causal_plan(const pcp_dims_t& d) {
 // `single`: the plan of the only launch, which wrote its single-segment
 // units as final output (rows the combine skips); null when every unit's
 // result is in the partials.
+// `count` / `count_dev`: the single launch's keys (dense) or key tiles (in
+// place, `count_is_tiles`), as its kernel saw them.
 int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int splits, void* out, cudaStream_t st,
-                   LaunchCounter* lc, const SplitPlan* single = nullptr, int64_t num_keys = 0,
-                   const int* num_keys_dev = nullptr) {
+                   LaunchCounter* lc, const SplitPlan* single = nullptr, int64_t count = 0,
+                   const int* count_dev = nullptr, bool count_is_tiles = false) {
   pcp::CombineParams p{};
   if (single) {
     p.skip_single = 1;
@@ -436,8 +498,9 @@ int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int spl
     p.grid_pairs = single->pairs;
     p.rows_per_head = static_cast<int>(rows_per_head(d));
     p.m_tiles = static_cast<int>(ceil_div(rows_per_head(d), pcp::kPairRows));
-    p.num_keys = static_cast<int>(num_keys);
-    p.num_keys_dev = num_keys_dev;
+    p.count = static_cast<int>(count);
+    p.count_dev = count_dev;
+    p.count_is_keys = count_is_tiles ? 0 : 1;
   }
   p.part_o = reinterpret_cast<const float*>(ws + w.po_off);
   p.part_lse = reinterpret_cast<const float*>(ws + w.pl_off);
@@ -454,26 +517,171 @@ int launch_combine(const pcp_dims_t& d, const Workspace& w, uint8_t* ws, int spl
   return PCP_OK;
 }
 
-// One attention "part" = a set of sources unpacked into a key range, then
-// attended in one launch.
+// One attention "part" = a set of history sources attended in one launch:
+// read in place from their cache blocks, or unpacked into a key range of the
+// dense workspace first.
 struct Part {
-  std::vector<pcp::UnpackSource> srcs;
-  int64_t key_off = 0;
+  bool in_place = false;
+  std::vector<pcp::UnpackSource> srcs;  // every source (dense path: what the unpack reads)
+  int64_t key_off = 0;                  // dense path: first workspace key
   int64_t keys = 0;
+  int64_t tiles = 0;                    // key tiles of the launch (or their bound)
   SplitPlan plan;
   bool last = true;  // the forward's last history launch (no exchange in flight)
   int sms = 0;       // SMs the launch may use (0: all); fewer leave SMs to an exchange in flight
+  // In place: the buffer holding the sources' blocks, its block count, and
+  // the block-table entries / first blocks of the sources.
+  const void* map_base = nullptr;
+  int64_t map_blocks = 0;
+  std::vector<pcp::KvSource> kv;
 };
+
+// Appends a history source of `valid` tokens (device-length mode: the bound)
+// to a part.  Dense path: an unpack source at the part's next key.  In
+// place: source `src` of the part's map, its logical block b at map block
+// blk0 + b or table[b].
+void add_source(const pcp_dims_t& d, Part* part, const uint8_t* base, const int32_t* table, int64_t pool_blocks,
+                int valid, int dev_index, bool device_lengths) {
+  const int64_t pay = payload_bytes(d);
+  if (valid > 0) {
+    const int64_t dst = device_lengths ? part->key_off : part->key_off + part->keys;
+    part->srcs.push_back(table ? paged_src(base, table, pool_blocks, valid, dst, dev_index)
+                               : contiguous_src(base, valid, dst, dev_index));
+    pcp::KvSource k{};
+    k.table = table;
+    k.blk0 = (table || !part->map_base) ? 0 : (base - static_cast<const uint8_t*>(part->map_base)) / pay;
+    k.valid = valid;
+    k.dev_index = dev_index;
+    part->kv.push_back(k);
+  }
+  part->keys += valid;
+  part->tiles += part->in_place ? ceil_div(valid, pcp::kTileN) : 0;
+}
+
+// Key tiles a part's launch walks: per source when in place, over the
+// compacted keys otherwise.
+int64_t part_tiles(const pcp_dims_t& d, const Part& part) {
+  return part.in_place ? part.tiles : ceil_div(part.keys, pcp::kTileN);
+}
 
 int plan_part(const pcp_dims_t& d, Part* part, int sms, int max_splits) {
   if (part->keys == 0) return PCP_OK;
   if (part->sms > 0 && part->sms < sms) {
     // A launch that shares the GPU with an exchange: a persistent grid on
     // part->sms SMs (stream-K; the caller checked that its K/V fits in L2).
-    part->plan = plan_stream_k(m_units(d), ceil_div(part->keys, pcp::kTileN), part->sms, max_splits);
+    part->plan = plan_stream_k(m_units(d), part_tiles(d, *part), part->sms, max_splits);
     return PCP_OK;
   }
-  part->plan = plan_splits(d, part->keys, sms, max_splits, part->last);
+  part->plan = plan_splits(d, part_tiles(d, *part), part->keys, sms, max_splits, part->last, part->in_place);
+  return PCP_OK;
+}
+
+// Attention over the e4m3 cache blocks of `part` read in place
+// (attn_fwd_kv_kernel).  Writes bf16 `out` directly (final, one segment per
+// unit) or split partials.  `tiles_dev` (device-length mode): where the
+// kernel stores the key tiles it walked, for the combine.
+int launch_attention_kv(const pcp_dims_t& d, const void* q, const Part& part, uint8_t* ws, const Workspace& w,
+                        int split_base, bool final_out, void* out, cudaStream_t st, LaunchCounter* lc,
+                        const int32_t* valid_dev = nullptr, int* tiles_dev = nullptr) {
+  const SplitPlan& plan = part.plan;
+  if (part.kv.size() > static_cast<size_t>(pcp::kMaxSources)) return fail(PCP_ERR_UNSUPPORTED, "too many sources");
+  const int64_t R = rows_per_head(d);
+  const int64_t mt = ceil_div(R, pcp::kPairRows);
+  CUtensorMap tq, tk, tv;
+  PCP_TRY(make_tmap(&tq, q, d.head_dim, R, d.num_kv_heads, R * d.head_dim));
+  PCP_TRY(make_tmap_blocks(&tk, part.map_base, d, part.map_blocks, d.head_dim));
+  PCP_TRY(make_tmap_blocks(&tv, part.map_base, d, part.map_blocks, d.head_dim / 2));
+  pcp::KvParams kp{};
+  pcp::AttnParams& p = kp.a;
+  p.rows_per_head = static_cast<int>(R);
+  p.m_tiles_per_head = static_cast<int>(mt);
+  p.num_kv_heads = d.num_kv_heads;
+  p.tiles_per_split = plan.tiles_per_split;
+  p.split_base = split_base;
+  p.total_rows = static_cast<int>(total_rows(d));
+  p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d.head_dim)) * 1.4426950408889634);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.max_segs = plan.splits;
+  p.final_ok = final_out ? 1 : 0;
+  p.part_o = reinterpret_cast<float*>(ws + w.po_off);
+  p.part_lse = reinterpret_cast<float*>(ws + w.pl_off);
+  p.err = reinterpret_cast<int*>(ws);
+  for (size_t i = 0; i < part.kv.size(); ++i) kp.src[i] = part.kv[i];
+  kp.num_sources = static_cast<int>(part.kv.size());
+  kp.block_size = d.block_size;
+  kp.map_blocks = part.map_blocks;
+  kp.valid_dev = valid_dev;
+  kp.tiles_out = tiles_dev;
+  const bool sk = plan.mode == kModeStreamK;
+  kp.sched = sk ? pcp::kSchedStreamK : pcp::kSchedStatic;
+  const dim3 grid = sk ? dim3(static_cast<unsigned>(2 * plan.pairs), 1)
+                       : dim3(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
+  static int done = 0;
+  if (d.head_dim == 256) {
+    PCP_TRY(set_smem_attr(pcp::attn_fwd_kv_kernel<256>, pcp::KvSmem<256>::kAlloc, &done));
+    pcp::attn_fwd_kv_kernel<256><<<grid, pcp::kKvThreads, pcp::KvSmem<256>::kAlloc, st>>>(tq, tk, tv, kp);
+  } else {
+    static int done128 = 0;
+    PCP_TRY(set_smem_attr(pcp::attn_fwd_kv_kernel<128>, pcp::KvSmem<128>::kAlloc, &done128));
+    pcp::attn_fwd_kv_kernel<128><<<grid, pcp::kKvThreads, pcp::KvSmem<128>::kAlloc, st>>>(tq, tk, tv, kp);
+  }
+  CUDA_TRY(cudaGetLastError());
+  if (lc) {
+    lc->kernels++;
+    lc->attn++;
+  }
+  return PCP_OK;
+}
+
+// The part of a stateless call: `num_sources` shards back to back in
+// `packed_kv`, `max_local_blocks` blocks each, source s with valid_len[s]
+// tokens.
+int packed_part(const pcp_dims_t& d, const void* packed_kv, int num_sources, const int32_t* valid_len, Part* part,
+                int mode) {
+  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
+  const int64_t pay = payload_bytes(d);
+  part->in_place = choose_in_place(d, mode);
+  part->map_base = packed_kv;
+  part->map_blocks = static_cast<int64_t>(num_sources) * d.max_local_blocks;
+  for (int s = 0; s < num_sources; ++s) {
+    if (valid_len[s] < 0 || valid_len[s] > cap)
+      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
+                  static_cast<long long>(cap));
+    if (valid_len[s] > 0 && !packed_kv) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL packed_kv");
+    add_source(d, part, static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
+               nullptr, 0, valid_len[s], -1, false);
+  }
+  return PCP_OK;
+}
+
+// Dense workspace keys of a history over `keys` keys: none when the cache is
+// read in place.
+int64_t dense_keys(int64_t keys, bool in_place) { return in_place ? 0 : keys; }
+
+// Plan of a stateless launch: made from the total key count alone (all the
+// workspace-size queries see), then fitted to the part's actual key tiles.
+SplitPlan stateless_plan(const pcp_dims_t& d, const Part& part, int slot_cap) {
+  const SplitPlan pl =
+      plan_splits(d, ceil_div(part.keys, pcp::kTileN), part.keys, num_sms(), slot_cap, true, part.in_place);
+  return fit_plan(pl, part_tiles(d, part));
+}
+
+// The launches of one stateless history part: its attention (in place, or
+// unpack + dense) writing bf16 `out` where one segment covers a unit, and
+// the combine when it left partials.
+int run_single_part(const pcp_dims_t& d, const void* q, const Part& part, const Workspace& w, uint8_t* ws, void* out,
+                    cudaStream_t st) {
+  const bool in_place = part.in_place;
+  if (in_place) {
+    PCP_TRY(launch_attention_kv(d, q, part, ws, w, 0, true, out, st, nullptr));
+  } else {
+    PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+    PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
+  }
+  if (part.plan.splits > 1)
+    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
+                           part.plan.mode == kModeStreamK ? &part.plan : nullptr,
+                           in_place ? part.tiles : part.keys, nullptr, in_place));
   return PCP_OK;
 }
 
@@ -522,6 +730,7 @@ struct pcp_handle {
   uint8_t* cur_k = nullptr;  // [P][Hkv][Qloc][D] bf16: current tokens' K of every rank (P > 1)
   uint8_t* cur_v = nullptr;
   int exchange = PCP_EXCHANGE_DIRECT;
+  int kv_path = -1;   // PCP_KV_PATH_* for this handle; -1: the process default
   int comm_sms = 16;  // SMs left to the direct exchange while the local shard is attended (P >= 4)
   uint8_t* ws = nullptr;
   Workspace w;
@@ -655,7 +864,12 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     total += valid_len[s];
   }
   if (total == 0 && !with_cur) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
-  if (total + (with_cur ? current_keys(d) : 0) > h->w.key_stride)
+  // How the history is read (the handle's setting, else the process
+  // default), and the dense workspace keys: the unpacked history (none in
+  // place), then the current tokens of a prefill.
+  const bool in_place = choose_in_place(d, h->kv_path >= 0 ? h->kv_path : g_kv_path.load());
+  const int64_t cur_off = dense_keys(total, in_place);
+  if (cur_off + (with_cur ? current_keys(d) : 0) > h->w.key_stride)
     return fail(PCP_ERR_UNSUPPORTED, "workspace holds %lld keys", static_cast<long long>(h->w.key_stride));
   CUDA_TRY(cudaSetDevice(h->device));
   h->last_stream = st;
@@ -668,12 +882,12 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   // once its shards have landed; their split partials meet in one combine.
   std::vector<Part> parts(1);
   std::vector<cudaEvent_t> ready(1, nullptr);  // event a part waits for (null: none)
+  parts[0].in_place = in_place;
   parts[0].key_off = 0;
-  parts[0].keys = valid_len[r];
-  if (valid_len[r] > 0)
-    parts[0].srcs.push_back(local.table
-                                ? paged_src(local.base, local.table, local.pool_blocks, valid_len[r], 0, r)
-                                : contiguous_src(local.base, valid_len[r], 0, r));
+  parts[0].map_base = local.base;
+  parts[0].map_blocks = local.table ? local.pool_blocks : d.max_local_blocks;
+  add_source(d, &parts[0], static_cast<const uint8_t*>(local.base), local.table, local.pool_blocks, valid_len[r], r,
+             valid_dev != nullptr);
   int64_t next_key = parts[0].keys;
   int64_t sent = 0;
   // Cleared before the ring stream starts: its block gather may report too.
@@ -712,16 +926,17 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
                                   h->comm_stream));
       own = dst;
     }
-    // Remote part over ring steps [s0, s1): sources (rank - s) % P, in ring order.
+    // Remote part over ring steps [s0, s1): sources (rank - s) % P, in ring
+    // order; in place, their blocks are read from the receive slots.
     auto add_part = [&](int s0, int s1, cudaEvent_t ev) {
       Part part;
+      part.in_place = in_place;
       part.key_off = next_key;
+      part.map_base = h->ring;
+      part.map_blocks = static_cast<int64_t>(P) * static_cast<int64_t>(slot_stride / pay);
       for (int step = s0; step < s1; ++step) {
         const int src = ((r - step) % P + P) % P;
-        if (valid_len[src] > 0)
-          part.srcs.push_back(valid_dev ? contiguous_src(slot(src), valid_len[src], part.key_off, src)
-                                        : contiguous_src(slot(src), valid_len[src], part.key_off + part.keys));
-        part.keys += valid_len[src];
+        add_source(d, &part, slot(src), nullptr, 0, valid_len[src], src, valid_dev != nullptr);
       }
       next_key += part.keys;
       parts.push_back(part);
@@ -793,9 +1008,8 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       //     1..ceil((P-1)/2), then the rest), the first group's shards
       //     attended while the second group's travel;
       //   * else one group (fewer launches and split partials).
-      const int64_t local_kv = static_cast<int64_t>(valid_len[r]) * d.num_kv_heads * d.head_dim * 4;
       const bool reserve = P >= 4 && h->comm_sms > 0 && h->comm_sms < h->sms && parts[0].keys > 0 &&
-                           local_kv <= kStreamKMaxKvBytes;
+                           kv_bytes(d, valid_len[r], in_place) <= kStreamKMaxKvBytes;
       if (reserve) parts[0].sms = h->sms - h->comm_sms;
       Part probe = parts[0];
       probe.last = false;
@@ -839,8 +1053,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   // where its K/V fits in L2.
   if (P > 1 && h->exchange == PCP_EXCHANGE_PIPELINE && h->comm_sms > 0 && h->comm_sms < h->sms)
     for (auto& part : parts)
-      if (part.keys && !part.last &&
-          part.keys * d.num_kv_heads * d.head_dim * 4 <= kStreamKMaxKvBytes)
+      if (part.keys && !part.last && kv_bytes(d, part.keys, in_place) <= kStreamKMaxKvBytes)
         part.sms = h->sms - h->comm_sms;
   int total_splits = 0;
   for (auto& part : parts) {
@@ -875,11 +1088,11 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   auto launch_current = [&]() -> int {
     if (P > 1) CUDA_TRY(cudaStreamWaitEvent(st, h->ev_cur, 0));
     int sp = prof_begin(h, 1, st);
-    PCP_TRY(launch_scatter(d, P > 1 ? h->cur_k : k_cur, P > 1 ? h->cur_v : v_cur, stripe_width, h->w, h->ws, total,
+    PCP_TRY(launch_scatter(d, P > 1 ? h->cur_k : k_cur, P > 1 ? h->cur_v : v_cur, stripe_width, h->w, h->ws, cur_off,
                            st, &lc));
     prof_end(h, sp, st);
     sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, total, current_keys(d), causal_plan(d), split_base, cur_only, out,
+    PCP_TRY(launch_attention(d, q, h->w, h->ws, cur_off, current_keys(d), causal_plan(d), split_base, cur_only, out,
                              st, &lc, Causal{r, stripe_width}));
     prof_end(h, sp, st);
     split_base += 1;
@@ -890,14 +1103,20 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     if (ready[i]) CUDA_TRY(cudaStreamWaitEvent(st, ready[i], 0));
     const Part& part = parts[i];
     if (!part.keys) continue;
-    int* keys_dev = valid_dev ? part_keys_slot(h->ws, static_cast<int>(i)) : nullptr;
-    int sp = prof_begin(h, 1, st);
-    PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc, valid_dev, keys_dev));
-    prof_end(h, sp, st);
-    sp = prof_begin(h, 2, st);
-    PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, single, out, st,
-                             &lc, Causal{}, keys_dev));
-    prof_end(h, sp, st);
+    int* count_dev = valid_dev ? part_keys_slot(h->ws, static_cast<int>(i)) : nullptr;
+    if (in_place) {
+      const int sp = prof_begin(h, 2, st);
+      PCP_TRY(launch_attention_kv(d, q, part, h->ws, h->w, split_base, single, out, st, &lc, valid_dev, count_dev));
+      prof_end(h, sp, st);
+    } else {
+      int sp = prof_begin(h, 1, st);
+      PCP_TRY(launch_unpack(d, part.srcs, h->w, h->ws, st, &lc, valid_dev, count_dev));
+      prof_end(h, sp, st);
+      sp = prof_begin(h, 2, st);
+      PCP_TRY(launch_attention(d, q, h->w, h->ws, part.key_off, part.keys, part.plan, split_base, single, out, st,
+                               &lc, Causal{}, count_dev));
+      prof_end(h, sp, st);
+    }
     split_base += part.plan.splits;
   }
   if (parts.size() == 1 && with_cur) PCP_TRY(launch_current());
@@ -906,8 +1125,8 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     const int only_idx = single ? static_cast<int>(only - parts.data()) : 0;
     const bool skip = single && only->plan.mode == kModeStreamK;
     PCP_TRY(launch_combine(d, h->w, h->ws, total_splits, out, st, &lc, skip ? &only->plan : nullptr,
-                           single ? only->keys : 0,
-                           single && valid_dev ? part_keys_slot(h->ws, only_idx) : nullptr));
+                           single ? (in_place ? only->tiles : only->keys) : 0,
+                           single && valid_dev ? part_keys_slot(h->ws, only_idx) : nullptr, in_place));
     prof_end(h, sp, st);
   }
   pcp_stats_t& L = h->last;
@@ -918,6 +1137,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
   L.forwards = 1;
   L.ring_bytes = sent;
   L.keys = total;
+  L.kv_in_place = in_place ? 1 : 0;
   if (h->profiling) {
     pcp_stats_t& A = h->accum;
     A.kernel_launches += lc.kernels;
@@ -926,6 +1146,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
     A.forwards += 1;
     A.ring_bytes += sent;
     A.keys = total;
+    A.kv_in_place = in_place ? 1 : 0;
   }
   return PCP_OK;
 }
@@ -974,8 +1195,10 @@ int pcp_history_attention_workspace_size(const pcp_dims_t* dims, int64_t total_v
   PCP_TRY(check_dims(dims));
   if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
   const int ms = max_splits_for(*dims);
-  const SplitPlan plan = plan_splits(*dims, total_valid, num_sms(), ms, true);
-  *bytes = ws_layout(*dims, total_valid, plan.splits).total;
+  const bool ip = choose_in_place(*dims, g_kv_path.load());
+  const SplitPlan plan =
+      plan_splits(*dims, ceil_div(total_valid, pcp::kTileN), total_valid, num_sms(), ms, true, ip);
+  *bytes = ws_layout(*dims, dense_keys(total_valid, ip), plan.splits).total;
   return PCP_OK;
 }
 
@@ -988,42 +1211,28 @@ int pcp_history_attention(const pcp_dims_t* dims, const void* q, const void* pac
     return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
   if (num_sources <= 0 || num_sources > pcp::kMaxSources)
     return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
-  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
-  const int64_t pay = payload_bytes(d);
   Part part;
-  for (int s = 0; s < num_sources; ++s) {
-    if (valid_len[s] < 0 || valid_len[s] > cap)
-      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
-                  static_cast<long long>(cap));
-    if (valid_len[s] > 0)
-      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
-                                         valid_len[s], part.keys));
-    part.keys += valid_len[s];
-  }
+  PCP_TRY(packed_part(d, packed_kv, num_sources, valid_len, &part, g_kv_path.load()));
   if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
-  const int sms = num_sms();
-  plan_part(d, &part, sms, max_splits_for(d));
-  const Workspace w = ws_layout(d, part.keys, part.plan.splits);
+  part.plan = stateless_plan(d, part, max_splits_for(d));
+  const Workspace w = ws_layout(d, dense_keys(part.keys, part.in_place), part.plan.splits);
   if (workspace_bytes < w.total)
     return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
   auto* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
-  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
-  if (part.plan.splits > 1)
-    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
-                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
-  return PCP_OK;
+  return run_single_part(d, q, part, w, ws, out, st);
 }
 
 int pcp_prefill_attention_workspace_size(const pcp_dims_t* dims, int64_t total_valid, size_t* bytes) {
   PCP_TRY(check_dims(dims));
   if (!bytes || total_valid < 0) return fail(PCP_ERR_INVALID_ARGUMENT, "bad arguments");
   int splits = 0;
+  const bool ip = choose_in_place(*dims, g_kv_path.load());
   if (total_valid > 0)
-    splits = plan_splits(*dims, total_valid, num_sms(), max_splits_for(*dims) - 1, true).splits;
-  *bytes = ws_layout(*dims, total_valid + current_keys(*dims), splits + 1).total;
+    splits = plan_splits(*dims, ceil_div(total_valid, pcp::kTileN), total_valid, num_sms(),
+                         max_splits_for(*dims) - 1, true, ip).splits;
+  *bytes = ws_layout(*dims, dense_keys(total_valid, ip) + current_keys(*dims), splits + 1).total;
   return PCP_OK;
 }
 
@@ -1038,27 +1247,17 @@ int pcp_prefill_attention(const pcp_dims_t* dims, int32_t interleave_size, int32
   if (rank < 0 || rank >= d.pcp_size) return fail(PCP_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, d.pcp_size);
   if (num_sources < 0 || num_sources > pcp::kMaxSources)
     return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [0, %d]", num_sources, pcp::kMaxSources);
-  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
-  const int64_t pay = payload_bytes(d);
   Part part;
-  for (int s = 0; s < num_sources; ++s) {
-    if (valid_len[s] < 0 || valid_len[s] > cap)
-      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
-                  static_cast<long long>(cap));
-    if (valid_len[s] > 0) {
-      if (!packed_kv) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL packed_kv");
-      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
-                                         valid_len[s], part.keys));
-    }
-    part.keys += valid_len[s];
-  }
-  const int sms = num_sms();
+  PCP_TRY(packed_part(d, packed_kv, num_sources, valid_len, &part, g_kv_path.load()));
   int splits = 0;
   if (part.keys) {
-    plan_part(d, &part, sms, max_splits_for(d) - 1);
+    part.plan = stateless_plan(d, part, max_splits_for(d) - 1);
     splits = part.plan.splits;
   }
-  const Workspace w = ws_layout(d, part.keys + current_keys(d), splits + 1);
+  // The current tokens go to the dense workspace after the dense history
+  // keys (none when the history is read in place).
+  const int64_t cur_off = dense_keys(part.keys, part.in_place);
+  const Workspace w = ws_layout(d, cur_off + current_keys(d), splits + 1);
   if (workspace_bytes < w.total)
     return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
   auto* ws = static_cast<uint8_t*>(workspace);
@@ -1066,11 +1265,15 @@ int pcp_prefill_attention(const pcp_dims_t* dims, int32_t interleave_size, int32
   const bool direct = splits == 0;
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
   if (part.keys) {
-    PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-    PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, false, out, st, nullptr));
+    if (part.in_place) {
+      PCP_TRY(launch_attention_kv(d, q, part, ws, w, 0, false, out, st, nullptr));
+    } else {
+      PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
+      PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, false, out, st, nullptr));
+    }
   }
-  PCP_TRY(launch_scatter(d, k_cur_all, v_cur_all, interleave_size, w, ws, part.keys, st, nullptr));
-  PCP_TRY(launch_attention(d, q, w, ws, part.keys, current_keys(d), causal_plan(d), splits, direct, out, st, nullptr,
+  PCP_TRY(launch_scatter(d, k_cur_all, v_cur_all, interleave_size, w, ws, cur_off, st, nullptr));
+  PCP_TRY(launch_attention(d, q, w, ws, cur_off, current_keys(d), causal_plan(d), splits, direct, out, st, nullptr,
                            Causal{rank, interleave_size}));
   if (!direct) PCP_TRY(launch_combine(d, w, ws, splits + 1, out, st, nullptr));
   return PCP_OK;
@@ -1088,29 +1291,25 @@ int pcp_history_attention_paged(const pcp_dims_t* dims, const void* q, const voi
     return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
   const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
   Part part;
+  part.in_place = choose_in_place(d, g_kv_path.load());
+  part.map_base = cache_pool;
+  part.map_blocks = pool_blocks;
   for (int s = 0; s < num_sources; ++s) {
     if (valid_len[s] < 0 || valid_len[s] > cap)
       return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
                   static_cast<long long>(cap));
-    if (valid_len[s] > 0)
-      part.srcs.push_back(paged_src(cache_pool, block_tables + static_cast<size_t>(s) * d.max_local_blocks, pool_blocks,
-                                    valid_len[s], part.keys));
-    part.keys += valid_len[s];
+    add_source(d, &part, static_cast<const uint8_t*>(cache_pool),
+               block_tables + static_cast<size_t>(s) * d.max_local_blocks, pool_blocks, valid_len[s], -1, false);
   }
   if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
-  plan_part(d, &part, num_sms(), max_splits_for(d));
-  const Workspace w = ws_layout(d, part.keys, part.plan.splits);
+  part.plan = stateless_plan(d, part, max_splits_for(d));
+  const Workspace w = ws_layout(d, dense_keys(part.keys, part.in_place), part.plan.splits);
   if (workspace_bytes < w.total)
     return fail(PCP_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu required", workspace_bytes, w.total);
   auto* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
-  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
-  if (part.plan.splits > 1)
-    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
-                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
-  return PCP_OK;
+  return run_single_part(d, q, part, w, ws, out, st);
 }
 
 int pcp_cache_write(const pcp_dims_t* dims, int32_t interleave_size, int32_t rank, int64_t first_position,
@@ -1226,36 +1425,35 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
     return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
   if (num_sources <= 0 || num_sources > pcp::kMaxSources)
     return fail(PCP_ERR_INVALID_ARGUMENT, "num_sources %d outside [1, %d]", num_sources, pcp::kMaxSources);
-  const int64_t cap = static_cast<int64_t>(d.max_local_blocks) * d.block_size;
-  const int64_t pay = payload_bytes(d);
-  Part part;
-  for (int s = 0; s < num_sources; ++s) {
-    if (valid_len[s] < 0 || valid_len[s] > cap)
-      return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d]=%d outside [0, %lld]", s, valid_len[s],
-                  static_cast<long long>(cap));
-    if (valid_len[s] > 0)
-      part.srcs.push_back(contiguous_src(static_cast<const uint8_t*>(packed_kv) + static_cast<size_t>(s) * d.max_local_blocks * pay,
-                                         valid_len[s], part.keys));
-    part.keys += valid_len[s];
-  }
-  if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
   // The largest split plan whose workspace fits the fixed scratch (a cap
   // that starves stream-K of pairs falls back to the static schedule inside
-  // plan_splits).
+  // plan_splits).  When the dense path chosen by default does not fit, an
+  // e4m3 cache is read in place instead (no dense copy in the scratch).
   const int sms = num_sms();
-  int split_cap = max_splits_for(d);
+  Part part;
   Workspace w;
-  while (true) {
-    part.plan = plan_splits(d, part.keys, sms, split_cap, true);
-    w = ws_layout(d, part.keys, part.plan.splits);
-    if (w.total <= PCP_NOALLOC_SCRATCH_BYTES) break;
-    if (part.plan.splits == 1)
-      return fail(PCP_ERR_UNSUPPORTED,
-                  "problem needs %zu scratch bytes; the allocation-free entry has %u (use pcp_history_attention "
-                  "with a caller workspace)",
-                  w.total, PCP_NOALLOC_SCRATCH_BYTES);
-    split_cap = part.plan.splits - 1;
-  }
+  auto fit = [&](int mode) -> int {
+    part = Part{};
+    PCP_TRY(packed_part(d, packed_kv, num_sources, valid_len, &part, mode));
+    if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
+    int split_cap = max_splits_for(d);
+    while (true) {
+      part.plan = plan_splits(d, part_tiles(d, part), part.keys, sms, split_cap, true, part.in_place);
+      w = ws_layout(d, dense_keys(part.keys, part.in_place), part.plan.splits);
+      if (w.total <= PCP_NOALLOC_SCRATCH_BYTES) return PCP_OK;
+      if (part.plan.splits == 1)
+        return fail(PCP_ERR_UNSUPPORTED,
+                    "problem needs %zu scratch bytes; the allocation-free entry has %u (use pcp_history_attention "
+                    "with a caller workspace)",
+                    w.total, PCP_NOALLOC_SCRATCH_BYTES);
+      split_cap = part.plan.splits - 1;
+    }
+  };
+  const int mode = g_kv_path.load();
+  int rc = fit(mode);
+  if (rc == PCP_ERR_UNSUPPORTED && !part.in_place && mode != PCP_KV_PATH_DENSE && kv_in_place_ok(d))
+    rc = fit(PCP_KV_PATH_IN_PLACE);
+  PCP_TRY(rc);
   void* scratch = nullptr;
   PCP_TRY(noalloc_scratch(&scratch));
   auto* ws = static_cast<uint8_t*>(scratch);
@@ -1264,11 +1462,7 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
   // K/V rows past num_keys are never read (TMA zero-fills past the tensor
   // map's extent) and every partial the combine reads is rewritten.
   CUDA_TRY(cudaMemsetAsync(ws, 0, 4, st));
-  PCP_TRY(launch_unpack(d, part.srcs, w, ws, st, nullptr));
-  PCP_TRY(launch_attention(d, q, w, ws, 0, part.keys, part.plan, 0, true, out, st, nullptr));
-  if (part.plan.splits > 1)
-    PCP_TRY(launch_combine(d, w, ws, part.plan.splits, out, st, nullptr,
-                           part.plan.mode == kModeStreamK ? &part.plan : nullptr, part.keys));
+  PCP_TRY(run_single_part(d, q, part, w, ws, out, st));
   CUDA_TRY(cudaMemcpyAsync(device_status, ws, sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
   return PCP_OK;
 }
@@ -1292,6 +1486,8 @@ int pcp_create(const pcp_dims_t* dims, int32_t rank, int32_t device, const void*
     return code;
   };
   // Dense keys: every source's history plus the current tokens of a prefill.
+  // Dense keys for every source (the handle may read either way; see
+  // pcp_set_kv_path) plus the current tokens of a prefill.
   const int64_t key_cap = static_cast<int64_t>(d.pcp_size) * d.max_local_blocks * d.block_size + current_keys(d);
   h->w = ws_layout(d, key_cap, max_splits_for(d));
   if (cudaMalloc(&h->ws, h->w.total) != cudaSuccess)
@@ -1482,6 +1678,16 @@ int pcp_stream_k_segments(int32_t units, int32_t key_tiles, int32_t grid_pairs, 
   }
   *count = n;
   return n > max_segments ? fail(PCP_ERR_INVALID_ARGUMENT, "%d segments, room for %d", n, max_segments) : PCP_OK;
+}
+
+int pcp_set_kv_path(pcp_handle_t* h, int32_t mode) {
+  if (mode != PCP_KV_PATH_AUTO && mode != PCP_KV_PATH_DENSE && mode != PCP_KV_PATH_IN_PLACE)
+    return fail(PCP_ERR_INVALID_ARGUMENT, "kv path %d unknown", mode);
+  if (h)
+    h->kv_path = mode;
+  else
+    g_kv_path.store(mode);
+  return PCP_OK;
 }
 
 int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms) {

@@ -98,6 +98,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int3
       : "memory");
 }
 
+// 5-D tiled load global -> THIS CTA's shared memory, completion on `bar` (an
+// mbarrier of this CTA).  Plain load of local-GPU memory; no multicast.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, int32_t c4, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+
 // 3-D tiled store shared -> global (bulk-group completion).
 __device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int32_t x, int32_t y, int32_t z) {
   asm volatile(
@@ -114,6 +125,21 @@ __device__ __forceinline__ void tma_store_wait_read0() {
 }
 
 __device__ __forceinline__ void tma_store_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 16-byte shared-memory load / store at a shared::cta address.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 // Make generic-proxy writes to shared memory visible to the async proxy (TMA
 // store / tcgen05.mma operand reads).
@@ -233,6 +259,13 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_m
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Same with f16 A and B (A/B format 0).  A and B of one kind::f16 MMA always
+// share a type: every operand of an f16 MMA here is f16.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // --------------------------------------------- CTA pairs (cta_group::2) ----
 // A cluster of two CTAs on two SMs shares one MMA: the leader (rank 0)
 // issues tcgen05.mma.cta_group::2, A comes from each CTA's own smem/TMEM
@@ -333,6 +366,49 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Two fp32 -> packed f16x2 (round to nearest even); `lo` lands in bits [0,16).
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Two e4m3fn bytes (low byte = first element) -> packed f16x2, exactly: every
+// e4m3fn value, NaN included, is representable in f16.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\t"
+      "cvt.u16.u32 t, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}"
+      : "=r"(r)
+      : "r"(two));
+  return r;
+}
+
+// Four e4m3fn bytes -> two packed f16x2 (bytes 0,1 -> a; bytes 2,3 -> b).
+__device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t w, uint32_t& a, uint32_t& b) {
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(a), "=r"(b)
+      : "r"(w));
+}
+
+// 16 e4m3fn bytes -> 16 f16 (two 16-byte chunks, element order kept).
+__device__ __forceinline__ void e4m3x16_to_f16(const uint4& in, uint4& lo, uint4& hi) {
+  e4m3x4_to_f16x4(in.x, lo.x, lo.y);
+  e4m3x4_to_f16x4(in.y, lo.z, lo.w);
+  e4m3x4_to_f16x4(in.z, hi.x, hi.y);
+  e4m3x4_to_f16x4(in.w, hi.z, hi.w);
+}
+
+// bf16x2 -> f16x2 (exact for magnitudes in f16's normal range, 2^-14 ..
+// 65504; smaller ones become f16 subnormals, larger ones +-inf).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t two) {
+  return pack_f16x2(__uint_as_float(two << 16), __uint_as_float(two & 0xFFFF0000u));
 }
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {

@@ -119,6 +119,10 @@ class HistoryAttention:
     ring step, each step's shard attended as soon as it lands).
     ``comm_sms`` (default 16) is how many SMs the local-shard launch leaves to
     the direct exchange when ``pcp_size >= 4`` (``pcp_set_comm_sms``).
+    ``kv_path`` picks how the KV cache is read (``pcp_set_kv_path``):
+    ``"dense"`` (a dense bf16 copy per forward), ``"in_place"`` (e4m3 blocks
+    read by TMA and upcast in shared memory) or ``"auto"``; None keeps the
+    process default (``_capi.set_default_kv_path``).
     """
 
     def __init__(
@@ -130,6 +134,7 @@ class HistoryAttention:
         group=None,
         exchange: str = "direct",
         comm_sms: int | None = None,
+        kv_path: str | None = None,
     ):
         self.config = config
         self.kv_dtype = kv_dtype
@@ -171,6 +176,12 @@ class HistoryAttention:
         self.exchange = exchange
         if comm_sms is not None:
             _capi.check(lib.pcp_set_comm_sms(self._handle, int(comm_sms)))
+        if kv_path is not None:
+            if kv_path not in _capi.KV_PATHS:
+                self.close()
+                raise ValueError(f"kv_path must be one of {sorted(_capi.KV_PATHS)}, got {kv_path!r}")
+            _capi.check(lib.pcp_set_kv_path(self._handle, _capi.KV_PATHS[kv_path]))
+        self.kv_path = kv_path or "default"
 
     # -- calls -------------------------------------------------------------
     def _check_inputs(self, q: torch.Tensor, packed_kv: torch.Tensor) -> None:

@@ -64,9 +64,10 @@ def load_peaks() -> dict:
     return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
-def load_profile_traffic(workload: str, n: int):
-    """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / f"attn_pair_{workload}_p{n}_traffic.txt"
+def load_profile_traffic(kernel: str, workload: str, n: int):
+    """DRAM bytes per attention launch from the committed ncu summary of this
+    kernel and workload, if any."""
+    p = ROOT / "profiles" / f"{kernel}_{workload}_p{n}_traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -268,7 +269,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
                                            device=dev)
     valid = cfg.source_valid_lens()
     attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=local_rank, exchange=args.exchange,
-                            comm_sms=args.comm_sms)
+                            comm_sms=args.comm_sms, kv_path=args.kv_path)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream()
     flops_step = 4.0 * cfg.num_q_heads * cfg.current_len * cfg.actual_history_len * cfg.head_dim
@@ -302,11 +303,14 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
     barrier()
     torch.cuda.synchronize()
     attn.set_profiling(True)
-    # A working set smaller than L2 would be served from L2 from the second
-    # step on: then L2 is flushed (a 256 MiB write) before every step, outside
-    # the step's events, and the time is the sum of the steps.
-    working_set = 2 * cfg.num_kv_heads * sum(valid) * cfg.head_dim * 2
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if working_set < L2_BYTES else None
+    # A working set that is not well above L2 would be served partly from L2
+    # from the second step on: then L2 is flushed (a 256 MiB write) before
+    # every step, outside the step's events, and the time is the sum of the
+    # steps.  e4m3 K/V is read in place (1 byte per element); a bf16 cache is
+    # read as is (2 bytes).
+    kv_elt = 1 if wl["kv"] == "e4m3" else 2
+    working_set = 2 * cfg.num_kv_heads * sum(valid) * cfg.head_dim * kv_elt
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if working_set < 2 * L2_BYTES else None
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -377,7 +381,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
         attn_ms_avg = st["attn_ms"] / max(st["attn_launches"], 1)
         attn_flops_launch = flops_rank * st["forwards"] / max(st["attn_launches"], 1)
         achieved = attn_flops_launch / (attn_ms_avg / 1e3) / 1e12 if attn_ms_avg > 0 else None
-        traffic = load_profile_traffic(args.workload, world)
+        traffic = load_profile_traffic("attn_kv" if st["kv_in_place"] else "attn_pair", args.workload, world)
         ring = None
         if world > 1 and st["forwards"]:
             per_fwd_bytes = st["ring_bytes"] / st["forwards"]
@@ -412,13 +416,16 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
                 "interleave_size": cfg.interleave_size,
                 "kv_dtype": wl["kv"],
                 "parallelism": f"pcp{world} (context-parallel, KV shards exchanged '{args.exchange}' over NVLink)",
-                "l2": ("inputs larger than L2" if flush is None else
+                "l2": ("inputs larger than twice L2" if flush is None else
                        "L2 flushed before every step (256 MiB write, outside the timed steps)")
-                      + f" (per rank: bf16 K/V working set {working_set / 2**20:.0f} MiB)",
+                      + f" (per rank: K/V working set {working_set / 2**20:.0f} MiB)",
             },
             "roofline": {
-                "kernel": "attn_fwd_pair_kernel / attn_fwd_pair_sk_kernel (CTA-pair tcgen05 QK^T / PV, "
-                          "TMEM accumulators), all attention launches of a step",
+                "kernel": ("attn_fwd_kv_kernel (e4m3 cache read in place by TMA, f16 upcast in shared memory, "
+                           "CTA-pair tcgen05 QK^T / PV, TMEM accumulators)" if st["kv_in_place"] else
+                           "attn_fwd_pair_kernel / attn_fwd_pair_sk_kernel (dense bf16 K/V unpacked once per "
+                           "forward, CTA-pair tcgen05 QK^T / PV, TMEM accumulators)") + ", all attention launches of a step",
+                "kv_path": "in_place" if st["kv_in_place"] else "dense",
                 "bound": "tensor",
                 "achieved": achieved,
                 "peak": peaks["bf16"],
@@ -641,6 +648,9 @@ def main() -> int:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--exchange", choices=("direct", "ring", "allgather", "pipeline"), default="direct")
+    ap.add_argument("--kv-path", choices=("auto", "dense", "in_place"), default=None,
+                    help="how the KV cache is read: dense bf16 copy, in place (e4m3, upcast in shared memory) "
+                         "or the library's automatic choice (default)")
     ap.add_argument("--comm-sms", type=int, default=None,
                     help="SMs the local-shard launch leaves to the exchange at 4+ ranks (library default 16)")
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define PCP_ATTN_ABI_VERSION 1
+#define PCP_ATTN_ABI_VERSION 2
 
 enum pcp_kv_dtype {
   PCP_KV_E4M3 = 0, /* float8_e4m3fn, dequantised at unit scale (reference.py:29-31) */
@@ -79,6 +79,8 @@ typedef struct pcp_stats {
   int32_t forwards;        /* forwards accumulated */
   int64_t ring_bytes;      /* bytes this rank sent around the ring */
   int64_t keys;            /* valid history keys attended by the last forward */
+  int32_t kv_in_place;     /* 1: the last forward read the cache in place (pcp_set_kv_path) */
+  int32_t reserved;
 } pcp_stats_t;
 
 typedef struct pcp_handle pcp_handle_t;
@@ -207,8 +209,9 @@ int pcp_selftest_bounded_wait(int32_t limit_us, int32_t* device_status);
  * forbidden or unsafe (inside a host framework that owns every byte of
  * device memory, a real-time serving loop that must never hit the allocator,
  * a plugin whose host forbids allocation).  Same computation and arguments as
- * pcp_history_attention, but the scratch (error word, dense bf16 K/V, split
- * partials) lives in a fixed static device array of
+ * pcp_history_attention, but the scratch (error word, split partials, and
+ * for a bf16 cache its dense bf16 copy; an e4m3 cache is read in place) lives
+ * in a fixed static device array of
  * PCP_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that loads
  * the library holds until the process exits.  The caller still passes the
  * inputs and the output, plus `device_status`: a caller-owned DEVICE int32
@@ -313,6 +316,29 @@ int pcp_set_exchange(pcp_handle_t* h, int32_t mode);
  * (the exchange then goes in two groups when the local launch fills the
  * GPU).  Default 16; rounded down to whole SM pairs. */
 int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms);
+
+/* How history launches read the KV cache.  No counterpart in the reference
+ * (its NKI kernel always loads the fp8 blocks into SBUF and upcasts there,
+ * kernel.py:295-339); both paths compute the same attention.
+ *   PCP_KV_PATH_DENSE -- the valid tokens are first expanded into a dense
+ *     bf16 workspace (one pass per forward), which the attention reads;
+ *   PCP_KV_PATH_IN_PLACE -- e4m3 caches with block_size % 64 == 0 are read
+ *     straight from their cache blocks (TMA) and upcast to f16 in shared
+ *     memory: no extra pass, no dense copy, but each 256-row query unit
+ *     converts every key tile again (other caches use the dense path);
+ *   PCP_KV_PATH_AUTO (default) -- in place when a KV head has at most 1024
+ *     query rows, dense otherwise (the allocation-free entry also reads in
+ *     place when the dense copy would not fit its scratch).
+ * h == NULL sets the process default, used by the stateless entries and by
+ * handles without their own setting.  The stateless entries size their
+ * workspace for the path in force when queried: keep the default unchanged
+ * between the workspace-size query and the call. */
+enum pcp_kv_path {
+  PCP_KV_PATH_AUTO = 0,
+  PCP_KV_PATH_DENSE = 1,
+  PCP_KV_PATH_IN_PLACE = 2
+};
+int pcp_set_kv_path(pcp_handle_t* h, int32_t mode);
 
 int pcp_set_profiling(pcp_handle_t* h, int32_t enable);
 int pcp_get_stats(const pcp_handle_t* h, pcp_stats_t* out);

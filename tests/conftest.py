@@ -25,3 +25,17 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(params=["dense", "in_place"])
+def kv_path(request):
+    """Runs a test with each way of reading the KV cache as the process
+    default (pcp_set_kv_path(NULL, ...)); e4m3 caches take it, bf16 caches
+    always use the dense path.  Restores the automatic choice afterwards."""
+    from aws_training_study_b200 import _capi
+
+    _capi.set_default_kv_path(request.param)
+    try:
+        yield request.param
+    finally:
+        _capi.set_default_kv_path("auto")

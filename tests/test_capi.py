@@ -36,7 +36,7 @@ def test_library_exports_every_declared_function():
 
 def test_abi_version_and_error_channel():
     lib = _capi.lib()
-    assert lib.pcp_abi_version() == 1
+    assert lib.pcp_abi_version() == 2
     status = lib.pcp_ring_schedule(0, 4, 4, None, None, None, None)
     assert status == 1  # PCP_ERR_INVALID_ARGUMENT
     assert b"hop" in lib.pcp_last_error()
@@ -80,11 +80,29 @@ def test_ring_schedule_follows_reference_order(P):
 
 def test_workspace_size_is_host_only():
     lib = _capi.lib()
-    dims = _capi.PcpDims(1, 4096, 256, 512, 32, 2, 256, 0)
     n = ctypes.c_size_t()
+    # bf16 cache: dense bf16 K and V for 131072 keys x 2 heads x 256 dims
+    dims = _capi.PcpDims(1, 4096, 256, 512, 32, 2, 256, 1)
     _capi.check(lib.pcp_history_attention_workspace_size(ctypes.byref(dims), 131072, ctypes.byref(n)))
-    # dense bf16 K and V for 131072 keys x 2 heads x 256 dims
     assert n.value >= 2 * 2 * 131072 * 256 * 2
+    # e4m3 cache: by default a KV head with 65536 query rows reads a dense
+    # copy; read in place there is no dense copy (and one split at P=1: no
+    # partials either)
+    dims = _capi.PcpDims(1, 4096, 256, 512, 32, 2, 256, 0)
+    _capi.check(lib.pcp_history_attention_workspace_size(ctypes.byref(dims), 131072, ctypes.byref(n)))
+    assert n.value >= 2 * 2 * 131072 * 256 * 2
+    try:
+        _capi.set_default_kv_path("in_place")
+        _capi.check(lib.pcp_history_attention_workspace_size(ctypes.byref(dims), 131072, ctypes.byref(n)))
+        assert n.value < 1 << 20
+    finally:
+        _capi.set_default_kv_path("auto")
+    # a short query shard (16 x 64 rows per KV head) reads in place by default
+    small = _capi.PcpDims(1, 64, 256, 512, 32, 2, 256, 0)
+    _capi.check(lib.pcp_history_attention_workspace_size(ctypes.byref(small), 131072, ctypes.byref(n)))
+    assert n.value < 2 * 2 * 131072 * 256 * 2
+    with pytest.raises(_capi.PcpError, match="kv path"):
+        _capi.check(lib.pcp_set_kv_path(None, 7))
     bad = _capi.PcpDims(1, 4096, 256, 512, 32, 2, 96, 0)
     assert lib.pcp_history_attention_workspace_size(ctypes.byref(bad), 10, ctypes.byref(n)) == 2  # UNSUPPORTED
     assert b"head_dim" in lib.pcp_last_error()

@@ -43,12 +43,12 @@ def _check(cfg: PCPAttentionConfig, kv_dtype, outliers: float) -> dict:
     return m
 
 
-def test_configs3_qwen_full_history_fp8():
+def test_configs3_qwen_full_history_fp8(kv_path):
     """BASELINE configs[3] at one GPU: 32/2 heads, D=256, Q=4096, 131072 history."""
     _check(PCPAttentionConfig(1, 4096, 131072, 131072, 512, 64, 32, 2, 256), torch.float8_e4m3fn, 0.0)
 
 
-def test_configs4_long_gqa_outliers_unaligned():
+def test_configs4_long_gqa_outliers_unaligned(kv_path):
     """BASELINE configs[4] shape at one GPU: 64/8 heads, D=128, Q=8192,
     500000 of 524288 history tokens, 1 % of K/V entries x8."""
     _check(PCPAttentionConfig(1, 8192, 524288, 500000, 512, 64, 64, 8, 128), torch.float8_e4m3fn, 0.01)

@@ -35,7 +35,7 @@ def _expected(q, k, v, hist):
                                        oc.softmax_scale)
 
 
-def test_device_lengths_equal_host_lengths_at_the_bound(case):
+def test_device_lengths_equal_host_lengths_at_the_bound(case, kv_path):
     q, k, v, qd, packed = case
     attn = HistoryAttention(CFG, rank=0, device=0)
     for hist in (8192, 3000):
@@ -47,7 +47,7 @@ def test_device_lengths_equal_host_lengths_at_the_bound(case):
     attn.close()
 
 
-def test_device_lengths_below_the_bound(case):
+def test_device_lengths_below_the_bound(case, kv_path):
     q, k, v, qd, packed = case
     attn = HistoryAttention(CFG, rank=0, device=0)
     for hist in (1, 700, 4096, 6145):
@@ -58,7 +58,7 @@ def test_device_lengths_below_the_bound(case):
     attn.close()
 
 
-def test_graph_replays_every_length_in_its_bucket(case):
+def test_graph_replays_every_length_in_its_bucket(case, kv_path):
     q, k, v, qd, packed = case
     attn = HistoryAttention(CFG, rank=0, device=0)
     g = BucketGraph(attn, [6144], qd, packed)
@@ -73,7 +73,7 @@ def test_graph_replays_every_length_in_its_bucket(case):
     assert g.graph is None  # released with the handle
 
 
-def test_bucketed_wrapper_records_one_graph_per_bucket(case):
+def test_bucketed_wrapper_records_one_graph_per_bucket(case, kv_path):
     q, k, v, qd, packed = case
     attn = HistoryAttention(CFG, rank=0, device=0)
     b = BucketedHistoryAttention(attn, qd, packed, granularity_blocks=4)
@@ -87,7 +87,7 @@ def test_bucketed_wrapper_records_one_graph_per_bucket(case):
     attn.close()
 
 
-def test_length_above_bucket_is_reported(case):
+def test_length_above_bucket_is_reported(case, kv_path):
     q, k, v, qd, packed = case
     attn = HistoryAttention(CFG, rank=0, device=0)
     vd = torch.tensor([5000], dtype=torch.int32, device=DEV)

@@ -98,7 +98,7 @@ def test_out_of_pool_table_entry_is_reported_not_written():
 
 
 @pytest.mark.parametrize("kv_dtype", [torch.float8_e4m3fn, torch.bfloat16], ids=["e4m3", "bf16"])
-def test_paged_attention_equals_contiguous_and_oracle(kv_dtype):
+def test_paged_attention_equals_contiguous_and_oracle(kv_dtype, kv_path):
     cfg = PCPAttentionConfig(4, 1024, 8192, 5000, 512, 64, 16, 2, 256)
     oc = oracle_config(cfg)
     k, v = _history_bf16(cfg, seed=9)
@@ -127,7 +127,7 @@ def test_paged_attention_equals_contiguous_and_oracle(kv_dtype):
     assert_parity(paged, want, "paged")
 
 
-def test_handle_forward_paged_single_rank_equals_forward():
+def test_handle_forward_paged_single_rank_equals_forward(kv_path):
     cfg = PCPAttentionConfig(1, 1024, 4096, 3333, 512, 64, 32, 2, 256)
     k, v = _history_bf16(cfg, seed=5)
     pools, tables, expected = _gpu_pools(cfg, k, v, torch.float8_e4m3fn, seed=6)
@@ -140,3 +140,23 @@ def test_handle_forward_paged_single_rank_equals_forward():
     attn.status()
     assert torch.equal(a, b)
     attn.close()
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.float8_e4m3fn, torch.bfloat16], ids=["e4m3", "bf16"])
+def test_attention_table_entry_outside_pool_is_reported(kv_dtype, kv_path):
+    """A block-table entry outside the pool is reported as code 109 (device
+    status) and never read: the e4m3 path loads an in-pool block in its place,
+    the bf16 unpack skips it."""
+    from aws_training_study_b200._capi import PcpError
+
+    cfg = PCPAttentionConfig(1, 256, 2048, 2048, 512, 64, 8, 2, 128)
+    k, v = _history_bf16(cfg, seed=3)
+    pools, tables, _ = _gpu_pools(cfg, k, v, kv_dtype, seed=4)
+    bad = tables[0].clone().reshape(1, -1)
+    bad[0, 1] = pools[0].shape[0] + 5
+    q = torch.randn(cfg.num_q_heads, cfg.local_q_len, cfg.head_dim, device=DEV).to(torch.bfloat16)
+    with pytest.raises(PcpError, match="code 109"):
+        history_attention_paged_single(q, pools[0], bad.contiguous(), [2048], cfg)
+    # the context is still usable
+    good = history_attention_paged_single(q, pools[0], tables[0].reshape(1, -1).contiguous(), [2048], cfg)
+    assert torch.isfinite(good.float()).all()

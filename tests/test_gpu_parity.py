@@ -38,11 +38,20 @@ CASES = [
     ("gqa8_d128_ragged", PCPAttentionConfig(4, 1024, 8192, 5000, 512, 64, 16, 4, 128), torch.float8_e4m3fn, [0, 2]),
     # multi-head (no GQA), the official-ring benchmark's shape at small size
     ("mha_d128_bf16", PCPAttentionConfig(2, 1024, 2048, 2048, 512, 64, 8, 8, 128), torch.bfloat16, [0, 1]),
+    # BASELINE configs[0]'s shape (64-token blocks): in place, the two 64-key
+    # halves of a V tile come from two cache blocks
+    ("cfg1_bs64_d128", PCPAttentionConfig(4, 256, 1024, 1024, 64, 16, 8, 2, 128), torch.float8_e4m3fn, [0, 3]),
+    # ragged sources with 64-token blocks: partial key tiles at every source,
+    # some of them one key half only
+    ("ragged_bs64_d256", PCPAttentionConfig(4, 256, 2048, 1001, 64, 16, 8, 2, 256), torch.float8_e4m3fn,
+     [0, 1, 2, 3]),
+    # an e4m3 block size that is no multiple of 64: the dense unpack path
+    ("e4m3_bs32_unpack", PCPAttentionConfig(2, 256, 1024, 1000, 32, 16, 8, 2, 128), torch.float8_e4m3fn, [0, 1]),
 ]
 
 
 @pytest.mark.parametrize("name,cfg,kv_dtype,ranks", CASES, ids=[c[0] for c in CASES])
-def test_rank_matches_oracle(name, cfg, kv_dtype, ranks):
+def test_rank_matches_oracle(name, cfg, kv_dtype, ranks, kv_path):
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=1234, kv_dtype=kv_dtype)
     packed = packed_shards(cfg, k_shards, v_shards)
     for rank in ranks:
@@ -50,7 +59,7 @@ def test_rank_matches_oracle(name, cfg, kv_dtype, ranks):
         assert_parity(out, expected_rank_output(cfg, q, k, v, rank), f"{name} rank {rank}")
 
 
-def test_single_rank_handle_direct_output():
+def test_single_rank_handle_direct_output(kv_path):
     """P = 1 through the handle: one stream-K attention launch writes every
     unit one segment covers as bf16 output; the combine merges the rest."""
     cfg = PCPAttentionConfig(1, 1024, 4096, 4096, 512, 64, 32, 2, 256)
@@ -60,7 +69,9 @@ def test_single_rank_handle_direct_output():
     out = attn(q_shards[0].cuda(), packed)
     attn.status()
     st = attn.stats()
-    assert st["attn_launches"] == 1 and st["kernel_launches"] <= 3  # unpack, attention, combine
+    # unpack (dense path only), attention, combine
+    assert st["attn_launches"] == 1 and st["kernel_launches"] <= (2 if kv_path == "in_place" else 3)
+    assert st["kv_in_place"] == (kv_path == "in_place")
     assert_parity(out, expected_rank_output(cfg, q, k, v, 0), "p1 direct")
     attn.close()
 

@@ -37,7 +37,7 @@ def _stateless(cfg, q_shards, packed, kc_shards, vc_shards, rank, kv_dtype, with
 
 
 @pytest.mark.parametrize("name,cfg,kv_dtype,ranks", CASES, ids=[c[0] for c in CASES])
-def test_prefill_matches_oracle(name, cfg, kv_dtype, ranks):
+def test_prefill_matches_oracle(name, cfg, kv_dtype, ranks, kv_path):
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=21, kv_dtype=kv_dtype)
     k_cur, v_cur, kc_shards, vc_shards = make_current(cfg, seed=21)
     packed = packed_shards(cfg, k_shards, v_shards)
@@ -57,7 +57,7 @@ def test_causal_only_without_history():
                       f"causal-only rank {rank}")
 
 
-def test_handle_prefill_single_rank():
+def test_handle_prefill_single_rank(kv_path):
     cfg = CASES[0][1]
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=8)
     k_cur, v_cur, kc_shards, vc_shards = make_current(cfg, seed=8)

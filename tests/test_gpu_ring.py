@@ -18,7 +18,7 @@ CASES = {
 }
 
 
-def _ring_body(rank, world, name, exchange="direct"):
+def _ring_body(rank, world, name, exchange="direct", kv_path=None):
     import sys
     from pathlib import Path
 
@@ -33,12 +33,13 @@ def _ring_body(rank, world, name, exchange="direct"):
     torch.cuda.set_device(rank)
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=11, kv_dtype=kv_dtype)
     packed = packed_shards(cfg, k_shards, v_shards)
-    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=rank, exchange=exchange)
+    attn = HistoryAttention(cfg, kv_dtype=kv_dtype, rank=rank, device=rank, exchange=exchange, kv_path=kv_path)
     qd, kvd = q_shards[rank].cuda(), packed[rank].cuda()
     for _ in range(3):  # repeated calls reuse the ring buffers
         out = attn(qd, kvd)
     attn.status(120000)
     st = attn.stats()
+    assert kv_path is None or st["kv_in_place"] == (kv_path == "in_place")
     m = assert_parity(out, expected_rank_output(cfg, q, k, v, rank), f"{name} rank {rank}")
     attn.close()
     return {"metrics": m, "ring_bytes": st["ring_bytes"], "attn_launches": st["attn_launches"]}
@@ -62,6 +63,19 @@ def ring_ragged_allgather(rank, world):
 
 def ring_qwen_pipeline(rank, world):
     return _ring_body(rank, world, "qwen_d256_fp8", exchange="pipeline")
+
+
+# The e4m3 cache read in place from the receive slots (pcp_set_kv_path).
+def ring_qwen_inplace(rank, world):
+    return _ring_body(rank, world, "qwen_d256_fp8", kv_path="in_place")
+
+
+def ring_qwen_storeforward_inplace(rank, world):
+    return _ring_body(rank, world, "qwen_d256_fp8", exchange="ring", kv_path="in_place")
+
+
+def ring_qwen_pipeline_inplace(rank, world):
+    return _ring_body(rank, world, "qwen_d256_fp8", exchange="pipeline", kv_path="in_place")
 
 
 def prefill_ragged(rank, world):
@@ -93,7 +107,7 @@ def prefill_ragged(rank, world):
     return {"metrics": m, "ring_bytes": st["ring_bytes"], "attn_launches": st["attn_launches"]}
 
 
-def ring_paged(rank, world):
+def ring_paged(rank, world, kv_path=None):
     """Each rank's cache written by the GPU producer into a pool through a
     permuted block table, then attended through the handle's paged entry
     (its live blocks are gathered before the exchange)."""
@@ -125,7 +139,7 @@ def ring_paged(rank, world):
     assert int(st.item()) == 0
     oc = oracle_config(cfg)
     q_shard = torch.from_numpy(orc.shard_query(to_numpy_f32(q), oc)[rank]).to(torch.bfloat16).to(dev)
-    attn = HistoryAttention(cfg, rank=rank, device=rank)
+    attn = HistoryAttention(cfg, rank=rank, device=rank, kv_path=kv_path)
     for _ in range(2):
         out = attn.forward_paged(q_shard, pool, table)
     attn.status(120000)
@@ -138,7 +152,7 @@ def ring_paged(rank, world):
     return {"metrics": m, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
 
 
-def ring_graph(rank, world):
+def ring_graph(rank, world, kv_path=None):
     """A length-bucket CUDA graph that records the NCCL exchange, replayed
     for several history lengths inside its bucket."""
     import sys
@@ -156,7 +170,7 @@ def ring_graph(rank, world):
     torch.cuda.set_device(rank)
     q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=19)
     packed = packed_shards(cfg, k_shards, v_shards)
-    attn = HistoryAttention(cfg, rank=rank, device=rank)
+    attn = HistoryAttention(cfg, rank=rank, device=rank, kv_path=kv_path)
     qd, kvd = q_shards[rank].cuda(), packed[rank].cuda()
     lens = {h: [orc.source_valid_len(h, P, I, s) for s in range(P)] for h in (6000, 5121, 4100)}
     bucket = bucket_for(cfg, lens[6000], granularity_blocks=2)
@@ -175,9 +189,19 @@ def ring_graph(rank, world):
     return {"metrics": worst, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
 
 
+def ring_paged_inplace(rank, world):
+    return ring_paged(rank, world, kv_path="in_place")
+
+
+def ring_graph_inplace(rank, world):
+    return ring_graph(rank, world, kv_path="in_place")
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather",
-                                "prefill_ragged", "ring_paged", "ring_graph", "ring_qwen_pipeline"])
+                                "prefill_ragged", "ring_paged", "ring_graph", "ring_qwen_pipeline",
+                                "ring_qwen_inplace", "ring_qwen_storeforward_inplace", "ring_qwen_pipeline_inplace",
+                                "ring_paged_inplace", "ring_graph_inplace"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res

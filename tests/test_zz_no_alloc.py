@@ -92,7 +92,8 @@ def test_noalloc_matches_oracle_and_workspace_entry_twice_in_a_row():
 
 def test_noalloc_one_split_when_partials_do_not_fit():
     # 32 x 4096 query rows: one split's fp32 partials alone (128 MiB) exceed
-    # the 64 MiB scratch, while the dense K/V (32 MiB) fits.
+    # the 64 MiB scratch (the e4m3 cache itself is read in place), so the
+    # launch runs as one split writing the output directly.
     dev = torch.device("cuda", 0)
     cfg = PCPAttentionConfig(1, 4096, 16384, 16384, 512, 64, 32, 2, 256)
     g = torch.Generator(device=dev).manual_seed(11)
@@ -141,11 +142,14 @@ def test_noalloc_allocates_nothing():
 
 
 def test_noalloc_rejects_oversized_problems():
+    # A bf16 cache is attended from a dense bf16 copy in the scratch: 256 MiB
+    # here, four times the array.  (An e4m3 cache is read in place and needs
+    # scratch only for split partials.)
     dev = torch.device("cuda", 0)
     cfg = PCPAttentionConfig(1, 4096, 131072, 131072, 512, 64, 32, 2, 256)
-    dims = make_dims(cfg, torch.float8_e4m3fn)
+    dims = make_dims(cfg, torch.bfloat16)
     q = torch.zeros(cfg.num_q_heads, cfg.local_q_len, cfg.head_dim, dtype=torch.bfloat16, device=dev)
-    packed = torch.zeros(cfg.max_local_blocks, payload_elements(cfg), dtype=torch.uint8, device=dev)
+    packed = torch.zeros(cfg.max_local_blocks, payload_elements(cfg), dtype=torch.bfloat16, device=dev)
     out = torch.empty_like(q)
     dstatus = torch.zeros(1, dtype=torch.int32, device=dev)
     status = _capi.lib().pcp_history_attention_noalloc(
