@@ -27,6 +27,30 @@
 
 namespace pcp {
 
+// Thread roles of the dense-K/V pair kernels (this file and
+// attn_pair_sk.cuh) for head dim D: kWG softmax warpgroups, each owning
+// kTileN / kWG keys of every row of a tile and D / kWG columns of O, then the
+// TMA warp and the MMA warp.  Two at both head dims: four (32 keys each) ran
+// configs[4]'s D = 128 shape at 1000 TFLOP/s against 1049 with two -- the
+// softmax there is bound by its instruction throughput per sub-partition,
+// which more warps do not raise, not by one row's latency.
+template <int D>
+struct PairRoles {
+  static constexpr int kWG = 2;
+  static constexpr int kSoftmaxThreads = 128 * kWG;
+  static constexpr int kSoftmaxWarps = kSoftmaxThreads / 32;
+  static constexpr int kThreads = kSoftmaxThreads + 64;
+  static constexpr int kProducerWarp = kSoftmaxWarps;
+  static constexpr int kMmaWarp = kProducerWarp + 1;
+  static constexpr int kKeys = kTileN / kWG;  // keys per softmax thread per tile
+  static constexpr int kOCols = D / kWG;      // O columns per softmax thread
+  // TMEM column of the P (16-bit, two per column) of keys [16 kk, +16): each
+  // warpgroup packs its keys into the first half of its own S columns.
+  static __device__ __forceinline__ uint32_t p_col(int kk) {
+    return static_cast<uint32_t>((16 * kk / kKeys) * kKeys + (16 * kk % kKeys) / 2);
+  }
+};
+
 template <int D>
 struct PairSmem {
   static constexpr int kQBytes = D * 2 * kTileM;           // own 128 rows (D/64 boxes of 16 KB)
@@ -41,7 +65,7 @@ struct PairSmem {
   static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kRedOff = kMiscOff + 16;
-  static constexpr int kBytes = kRedOff + 2 * kSoftmaxWarpgroups * kTileM * 4;
+  static constexpr int kBytes = kRedOff + 2 * PairRoles<D>::kWG * kTileM * 4;
   static constexpr int kAlloc = kBytes;
   static_assert(kAlloc <= 232448, "exceeds the 227 KB of shared memory per CTA");
 };
@@ -53,12 +77,14 @@ constexpr int kSoftmaxWarps = kSoftmaxThreads / 32;
 
 // p.m_tiles_per_head counts 256-row pair tiles here.
 template <int D>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThreads, 1)
     attn_fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                          const AttnParams p) {
   using L = PairSmem<D>;
+  using R = PairRoles<D>;
   constexpr int NS = L::kStages;
+  constexpr int kWG = R::kWG;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -106,7 +132,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int kt1 = min(kt0 + p.tiles_per_split, n_key_tiles);
   const int n = kt1 - kt0;  // >= 1 on the host plan; <= 0 only for an empty split in device-length mode
 
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == R::kProducerWarp && lane == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_kv_full(s), 1);
@@ -114,17 +140,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_s_full(b), 1);
-      mbar_init(bar_p_full(b), 2 * kSoftmaxWarps);  // one arrive per softmax warp of both CTAs
+      mbar_init(bar_p_full(b), 2 * R::kSoftmaxWarps);  // one arrive per softmax warp of both CTAs
     }
     mbar_init(bar_o(0), 1);
     mbar_init(bar_o(1), 1);
     mbar_init(bar_td, 1);
-    mbar_init(bar_red(0), kSoftmaxThreads);
-    mbar_init(bar_red(1), kSoftmaxThreads);
+    mbar_init(bar_red(0), R::kSoftmaxThreads);
+    mbar_init(bar_red(1), R::kSoftmaxThreads);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == R::kMmaWarp) {
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish_pair();
   }
@@ -133,7 +159,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kProducerWarp) {
+  if (warp == R::kProducerWarp) {
     // ------------------------------------------------------ TMA producer --
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm_q);
@@ -183,7 +209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
+  } else if (warp == R::kMmaWarp) {
     // --------------------------------------------- MMA issuer (leader only) --
     if (leader && lane == 0 && n > 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kPairRows, kTileN, false, false);
@@ -218,12 +244,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t vbase = sStage + st * L::kStageBytes;
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {
-          // A = P: keys [0, 64) sit in TMEM columns [0, 32) of the S buffer and
-          // keys [64, 128) in columns [64, 96) (each softmax warpgroup writes
-          // inside its own S columns); 16 keys = 8 columns per step.
+          // A = P: each softmax warpgroup packed its keys into the first half
+          // of its own S columns (R::p_col); 16 keys = 8 columns per step.
           // B = V half, MN-major: 64-dim chunks 16 KB apart (LBO), 8-key
           // groups 1 KB apart (SBO); a 16-key step is 2 KB.
-          const uint32_t a_cols = kk * 8 + (kk >= 4 ? 32 : 0);
+          const uint32_t a_cols = R::p_col(kk);
           umma_ts_pair(tmem, p_tmem + a_cols, make_sw128_desc(vbase + kk * 2048, L::kVBox, 1024), idesc_pv,
                        (j > 0 || kk > 0) ? 1u : 0u);
         }
@@ -244,8 +269,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------------------------------- softmax / correction / epilogue --
-    constexpr int kHalfKeys = kTileN / kSoftmaxWarpgroups;  // 64
-    constexpr int kOCols = D / kSoftmaxWarpgroups;
+    constexpr int kHalfKeys = R::kKeys;  // keys of this warpgroup per tile
+    constexpr int kOCols = R::kOCols;
     const int wg = warp >> 2;
     const int row = threadIdx.x & (kTileM - 1);  // == TMEM lane
     const uint32_t t_row = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -294,8 +319,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
       float s[kHalfKeys];
-      tmem_ld32(t_s + wg * kHalfKeys, s);
-      tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
+#pragma unroll
+      for (int c32 = 0; c32 < kHalfKeys / 32; ++c32) tmem_ld32(t_s + wg * kHalfKeys + 32 * c32, s + 32 * c32);
       tmem_wait_ld();
       const int valid = key_limit - (kt0 + j) * kTileN - wg * kHalfKeys;
       if (valid < kHalfKeys) {
@@ -314,7 +339,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       // Publish this half's max (double-buffered by tile parity; a
       // warpgroup is at most one tile ahead of the other).
-      red[(b * kSoftmaxWarpgroups + wg) * kTileM + row] = pmax;
+      red[(b * kWG + wg) * kTileM + row] = pmax;
       mbar_arrive(bar_red(b));
       // Tiles after the first: compute P with the current reference max
       // before the other half's max is known -- it only matters when the
@@ -323,7 +348,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (j > 0) tile_sum = make_p(s, m_ref, t_s);
       ok = __all_sync(0xffffffffu, mbar_wait(bar_red(b), (j >> 1) & 1u, abort_flag, p.err, kErrWaitRed));
       if (!ok) break;
-      const float tmax = fmaxf(pmax, red[(b * kSoftmaxWarpgroups + (wg ^ 1)) * kTileM + row]);
+      float tmax = pmax;
+#pragma unroll
+      for (int w = 1; w < kWG; ++w) tmax = fmaxf(tmax, red[(b * kWG + (wg ^ w)) * kTileM + row]);
       const bool need = (tmax - m_ref) * sl2 > kRescaleThreshold;  // always true on the first tile
       const bool redo = __any_sync(0xffffffffu, need);
       float alpha = 1.f;
@@ -365,12 +392,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (ok)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar_o((n - 1) & 1), ((n - 1) >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
-    ok = named_bar_and(1, kSoftmaxThreads, ok && (*abort_flag == 0));
+    ok = named_bar_and(1, R::kSoftmaxThreads, ok && (*abort_flag == 0));
     if (ok) {
       tc_fence_after();
       red[wg * kTileM + row] = l;
-      named_bar_sync(2, kSoftmaxThreads);
-      const float l_tot = l + red[(wg ^ 1) * kTileM + row];
+      named_bar_sync(2, R::kSoftmaxThreads);
+      float l_tot = l;
+#pragma unroll
+      for (int w = 1; w < kWG; ++w) l_tot += red[(wg ^ w) * kTileM + row];
       const float inv_l = 1.f / l_tot;
       if (p.write_final) {
 #pragma unroll 1
@@ -393,7 +422,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        named_bar_sync(3, kSoftmaxThreads);
+        named_bar_sync(3, R::kSoftmaxThreads);
         if (threadIdx.x == 0 && row0 < p.rows_per_head) {  // no store of a tile wholly past the rows
           for (int box = 0; box < D / kBoxCols; ++box)
             tma_store_3d(&tm_o, sQ + box * kBoxBytes, box * kBoxCols, row0, head);
@@ -434,7 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();
-  if (warp == kMmaWarp) {
+  if (warp == R::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, kTmemCols);
   }

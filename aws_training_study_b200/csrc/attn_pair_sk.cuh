@@ -42,7 +42,7 @@ struct PairSmemSK {
   static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 2 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kRedOff = kMiscOff + 16;
-  static constexpr int kBytes = kRedOff + 2 * kSoftmaxWarpgroups * kTileM * 4;
+  static constexpr int kBytes = kRedOff + 2 * PairRoles<D>::kWG * kTileM * 4;
   static constexpr int kAlloc = kBytes;
   static_assert(kAlloc <= 232448, "exceeds the 227 KB of shared memory per CTA");
 };
@@ -99,11 +99,13 @@ struct Schedule {
 };
 
 template <int D>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThreads, 1)
     attn_fwd_pair_sk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   using L = PairSmemSK<D>;
+  using R = PairRoles<D>;
   constexpr int NS = L::kStages;
+  constexpr int kWG = R::kWG;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -149,7 +151,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return true;
   };
 
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == R::kProducerWarp && lane == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_kv_full(s), 1);
@@ -157,18 +159,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_s_full(b), 1);
-      mbar_init(bar_p_full(b), 2 * kSoftmaxWarps);  // one arrive per softmax warp of both CTAs
+      mbar_init(bar_p_full(b), 2 * R::kSoftmaxWarps);  // one arrive per softmax warp of both CTAs
     }
     mbar_init(bar_o(0), 1);
     mbar_init(bar_o(1), 1);
     mbar_init(bar_td, 1);
-    mbar_init(bar_red(0), kSoftmaxThreads);
-    mbar_init(bar_red(1), kSoftmaxThreads);
+    mbar_init(bar_red(0), R::kSoftmaxThreads);
+    mbar_init(bar_red(1), R::kSoftmaxThreads);
     mbar_init(bar_q_empty, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == R::kMmaWarp) {
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish_pair();
   }
@@ -177,7 +179,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kProducerWarp) {
+  if (warp == R::kProducerWarp) {
     // ------------------------------------------------------ TMA producer --
     if (lane == 0) {
       uint32_t c = 0;
@@ -243,7 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
+  } else if (warp == R::kMmaWarp) {
     // --------------------------------------------- MMA issuer (leader only) --
     if (leader && lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kPairRows, kTileN, false, false);
@@ -278,12 +280,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t vbase = sStage + st * L::kStageBytes;
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {
-          // A = P: keys [0, 64) sit in TMEM columns [0, 32) of the S buffer and
-          // keys [64, 128) in columns [64, 96) (each softmax warpgroup writes
-          // inside its own S columns); 16 keys = 8 columns per step.
-          // B = V half, MN-major: 64-dim chunks 16 KB apart (LBO), 8-key
-          // groups 1 KB apart (SBO); a 16-key step is 2 KB.
-          const uint32_t a_cols = kk * 8 + (kk >= 4 ? 32 : 0);
+          // A = P: each softmax warpgroup packed its keys into the first half
+          // of its own S columns (PairRoles::p_col); 16 keys = 8 columns per
+          // step.  B = V half, MN-major: 64-dim chunks 16 KB apart (LBO),
+          // 8-key groups 1 KB apart (SBO); a 16-key step is 2 KB.
+          const uint32_t a_cols = R::p_col(kk);
           umma_ts_pair(tmem, p_tmem + a_cols, make_sw128_desc(vbase + kk * 2048, L::kVBox, 1024), idesc_pv,
                        (!first || kk > 0) ? 1u : 0u);
         }
@@ -320,8 +321,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------------------------------- softmax / correction / epilogue --
-    constexpr int kHalfKeys = kTileN / kSoftmaxWarpgroups;  // 64
-    constexpr int kOCols = D / kSoftmaxWarpgroups;
+    constexpr int kHalfKeys = R::kKeys;  // keys of this warpgroup per tile
+    constexpr int kOCols = R::kOCols;
     const int wg = warp >> 2;
     const int row = threadIdx.x & (kTileM - 1);  // == TMEM lane
     const uint32_t t_row = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -383,8 +384,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
         float s[kHalfKeys];
-        tmem_ld32(t_s + wg * kHalfKeys, s);
-        tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
+#pragma unroll
+        for (int c32 = 0; c32 < kHalfKeys / 32; ++c32) tmem_ld32(t_s + wg * kHalfKeys + 32 * c32, s + 32 * c32);
         tmem_wait_ld();
         const int valid = key_limit - (sg.kt0 + j) * kTileN - wg * kHalfKeys;
         if (valid < kHalfKeys) {
@@ -403,7 +404,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
         // Publish this half's max (double-buffered by tile parity; a
         // warpgroup is at most one tile ahead of the other).
-        red[(b * kSoftmaxWarpgroups + wg) * kTileM + row] = pmax;
+        red[(b * kWG + wg) * kTileM + row] = pmax;
         mbar_arrive(bar_red(b));
         // Tiles after the first: compute P with the current reference max
         // before the other half's max is known -- it only matters when the
@@ -412,7 +413,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (j > 0) tile_sum = make_p(s, m_ref, t_s);
         ok = __all_sync(0xffffffffu, mbar_wait(bar_red(b), (jg >> 1) & 1u, abort_flag, p.err, kErrWaitRed));
         if (!ok) break;
-        const float tmax = fmaxf(pmax, red[(b * kSoftmaxWarpgroups + (wg ^ 1)) * kTileM + row]);
+        float tmax = pmax;
+#pragma unroll
+        for (int w = 1; w < kWG; ++w) tmax = fmaxf(tmax, red[(b * kWG + (wg ^ w)) * kTileM + row]);
         const bool need = (tmax - m_ref) * sl2 > kRescaleThreshold;  // always true on the first tile
         const bool redo = __any_sync(0xffffffffu, need);
         float alpha = 1.f;
@@ -455,7 +458,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t jl = J + n - 1;
         ok = __all_sync(0xffffffffu, mbar_wait(bar_o(jl & 1), (jl >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
       }
-      ok = named_bar_and(1, kSoftmaxThreads, ok && (*abort_flag == 0));
+      ok = named_bar_and(1, R::kSoftmaxThreads, ok && (*abort_flag == 0));
       if (!ok) return false;
       J += n;
       const bool live = rih < p.rows_per_head;
@@ -473,10 +476,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       red[wg * kTileM + row] = l;
-      named_bar_sync(2, kSoftmaxThreads);
-      const float l_tot = l + red[(wg ^ 1) * kTileM + row];
-      // Both halves read: the next segment may reuse the exchange slots.
-      named_bar_sync(2, kSoftmaxThreads);
+      named_bar_sync(2, R::kSoftmaxThreads);
+      float l_tot = l;
+#pragma unroll
+      for (int w = 1; w < kWG; ++w) l_tot += red[(wg ^ w) * kTileM + row];
+      // Every share read: the next segment may reuse the exchange slots.
+      named_bar_sync(2, R::kSoftmaxThreads);
       const float inv_l = 1.f / l_tot;
       if (final_out) {
         // Stream-K: sQ may already hold the next segment's Q; store directly.
@@ -528,7 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();
-  if (warp == kMmaWarp) {
+  if (warp == R::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, kTmemCols);
   }

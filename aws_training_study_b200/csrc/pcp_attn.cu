@@ -124,12 +124,13 @@ constexpr int64_t kStreamKMaxKvBytes = int64_t(48) << 20;
 //     attn_fwd_kv_kernel loads the cache blocks with TMA and upcasts them to
 //     f16 in shared memory -- no extra pass and no dense copy, but every
 //     256-row query unit converts every key tile again.
-// Measured at BASELINE configs[3] on one B200 (attention launch, TFLOP/s):
-// dense 1466 (+ a 0.1 ms unpack), in place 1296, in place with the
-// conversion skipped 1572.  The conversion therefore pays only while a
-// KV head has few query units: `auto` reads in place up to
-// kInPlaceMaxRows query rows per KV head.
-constexpr int64_t kInPlaceMaxRows = 1024;
+// Measured on one B200 with configs[3]'s heads and 131072-token history
+// (whole forward, TFLOP/s, dense / in place): 1024 query rows per KV head
+// 887 / 1053, 4096 rows 1115 / 1148, 16384 rows 1510 / 1279, 65536 rows
+// 1481 / 1257 (in place with the conversion skipped: 1572).  The
+// conversion pays while a KV head has few 256-row query units: `auto` reads
+// in place up to kInPlaceMaxRows query rows per KV head.
+constexpr int64_t kInPlaceMaxRows = 4096;
 std::atomic<int> g_kv_path{PCP_KV_PATH_AUTO};  // process default (pcp_set_kv_path(NULL, ...))
 
 bool kv_in_place_ok(const pcp_dims_t& d) { return d.kv_dtype == PCP_KV_E4M3 && d.block_size % 64 == 0; }
@@ -322,10 +323,10 @@ int launch_pair_kernel(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const 
   static int done = 0;
   if constexpr (kStreamK) {
     PCP_TRY(set_smem_attr(pcp::attn_fwd_pair_sk_kernel<D>, pcp::PairSmemSK<D>::kAlloc, &done));
-    pcp::attn_fwd_pair_sk_kernel<D><<<grid, pcp::kThreads, pcp::PairSmemSK<D>::kAlloc, st>>>(tq, tk, tv, p);
+    pcp::attn_fwd_pair_sk_kernel<D><<<grid, pcp::PairRoles<D>::kThreads, pcp::PairSmemSK<D>::kAlloc, st>>>(tq, tk, tv, p);
   } else {
     PCP_TRY(set_smem_attr(pcp::attn_fwd_pair_kernel<D>, pcp::PairSmem<D>::kAlloc, &done));
-    pcp::attn_fwd_pair_kernel<D><<<grid, pcp::kThreads, pcp::PairSmem<D>::kAlloc, st>>>(tq, tk, tv, to, p);
+    pcp::attn_fwd_pair_kernel<D><<<grid, pcp::PairRoles<D>::kThreads, pcp::PairSmem<D>::kAlloc, st>>>(tq, tk, tv, to, p);
   }
   return PCP_OK;
 }

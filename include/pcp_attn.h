@@ -326,8 +326,8 @@ int pcp_set_comm_sms(pcp_handle_t* h, int32_t sms);
  *     straight from their cache blocks (TMA) and upcast to f16 in shared
  *     memory: no extra pass, no dense copy, but each 256-row query unit
  *     converts every key tile again (other caches use the dense path);
- *   PCP_KV_PATH_AUTO (default) -- in place when a KV head has at most 1024
- *     query rows, dense otherwise (the allocation-free entry also reads in
+ *   PCP_KV_PATH_AUTO (default) -- in place when a KV head has at most 4096
+ *     query rows (num_q_heads / num_kv_heads * local_q_len), dense otherwise (the allocation-free entry also reads in
  *     place when the dense copy would not fit its scratch).
  * h == NULL sets the process default, used by the stateless entries and by
  * handles without their own setting.  The stateless entries size their
