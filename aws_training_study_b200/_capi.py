@@ -99,6 +99,8 @@ SIGNATURES = {
     "pcp_forward_paged": (_c.c_int, [_P, _P, _P, _c.c_int64, _P, _PI32, _P, _P]),
     "pcp_forward_prefill": (_c.c_int, [_P, _I32, _P, _P, _PI32, _P, _P, _P, _P]),
     "pcp_forward_host": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_forward_host_async": (_c.c_int, [_P, _P, _P, _PI32, _P, _P]),
+    "pcp_forward_host_wait": (_c.c_int, [_P]),
     "pcp_device_status": (_c.c_int, [_P, _I32]),
     "pcp_set_exchange": (_c.c_int, [_P, _I32]),
     "pcp_set_comm_sms": (_c.c_int, [_P, _I32]),

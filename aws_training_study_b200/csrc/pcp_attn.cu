@@ -735,10 +735,21 @@ struct pcp_handle {
   int comm_sms = 16;  // SMs left to the direct exchange while the local shard is attended (P >= 4)
   uint8_t* ws = nullptr;
   Workspace w;
-  // staging for pcp_forward_host
-  void* dq = nullptr;
-  void* dkv = nullptr;
-  void* dout = nullptr;
+  // Staging of the host-buffer entries: two slots of device Q, packed KV and
+  // O, so that one call's copies (H2D on h2d_stream, D2H on d2h_stream)
+  // overlap another call's forward.
+  struct HostSlot {
+    void* q = nullptr;
+    void* kv = nullptr;
+    void* out = nullptr;
+    cudaEvent_t loaded = nullptr;   // inputs copied in
+    cudaEvent_t done = nullptr;     // forward finished (inputs free, output written)
+    cudaEvent_t fetched = nullptr;  // output copied out
+    bool used = false;
+  };
+  HostSlot slots[2];
+  int next_slot = 0;
+  cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
   // Profiling: CUDA event pairs recorded around every launch (on the
   // stream it is launched on) while profiling is on; resolved lazily.
   bool profiling = false;
@@ -1575,29 +1586,68 @@ int pcp_forward_prefill(pcp_handle_t* h, int32_t interleave_size, const void* q,
   return forward_impl(h, q, local, valid_len, k_cur, v_cur, interleave_size, out, static_cast<cudaStream_t>(stream));
 }
 
-int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
-                     void* out_host, void* stream) {
+int pcp_forward_host_async(pcp_handle_t* h, const void* q_host, const void* packed_kv_host,
+                           const int32_t* valid_len, void* out_host, void* stream) {
   if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
   if (!q_host || !packed_kv_host || !valid_len || !out_host) return fail(PCP_ERR_INVALID_ARGUMENT, "NULL buffer");
   const pcp_dims_t& d = h->d;
-  CUDA_TRY(cudaSetDevice(h->device));
-  const size_t qbytes = static_cast<size_t>(d.num_q_heads) * d.local_q_len * d.head_dim * 2;
-  const size_t kvbytes = static_cast<size_t>(d.max_local_blocks) * payload_bytes(d);
-  if (!h->dq) {
-    CUDA_TRY(cudaMalloc(&h->dq, qbytes));
-    CUDA_TRY(cudaMalloc(&h->dkv, kvbytes));
-    CUDA_TRY(cudaMalloc(&h->dout, qbytes));
-  }
   const int r = h->rank;
   if (valid_len[r] < 0 || valid_len[r] > static_cast<int64_t>(d.max_local_blocks) * d.block_size)
     return fail(PCP_ERR_INVALID_ARGUMENT, "valid_len[%d] out of range", r);
+  CUDA_TRY(cudaSetDevice(h->device));
+  const size_t qbytes = static_cast<size_t>(d.num_q_heads) * d.local_q_len * d.head_dim * 2;
+  const size_t kvbytes = static_cast<size_t>(d.max_local_blocks) * payload_bytes(d);
+  if (!h->h2d_stream) {
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    CUDA_TRY(cudaStreamCreateWithPriority(&h->h2d_stream, cudaStreamNonBlocking, hi));
+    CUDA_TRY(cudaStreamCreateWithPriority(&h->d2h_stream, cudaStreamNonBlocking, hi));
+    for (auto& sl : h->slots) {
+      CUDA_TRY(cudaMalloc(&sl.q, qbytes));
+      CUDA_TRY(cudaMalloc(&sl.kv, kvbytes));
+      CUDA_TRY(cudaMalloc(&sl.out, qbytes));
+      CUDA_TRY(cudaEventCreateWithFlags(&sl.loaded, cudaEventDisableTiming));
+      CUDA_TRY(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+      CUDA_TRY(cudaEventCreateWithFlags(&sl.fetched, cudaEventDisableTiming));
+    }
+  }
+  auto& sl = h->slots[h->next_slot];
   const size_t live = static_cast<size_t>(ceil_div(valid_len[r], d.block_size)) * payload_bytes(d);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CUDA_TRY(cudaMemcpyAsync(h->dq, q_host, qbytes, cudaMemcpyHostToDevice, st));
-  if (live) CUDA_TRY(cudaMemcpyAsync(h->dkv, packed_kv_host, live, cudaMemcpyHostToDevice, st));
-  PCP_TRY(pcp_forward(h, h->dq, h->dkv, valid_len, h->dout, stream));
-  CUDA_TRY(cudaMemcpyAsync(out_host, h->dout, qbytes, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaStreamSynchronize(st));
+  // The slot's previous call must have finished its forward (which read q and
+  // sent kv) before new inputs land, and its output copy before the forward
+  // writes out again.
+  if (sl.used) CUDA_TRY(cudaStreamWaitEvent(h->h2d_stream, sl.done, 0));
+  CUDA_TRY(cudaMemcpyAsync(sl.q, q_host, qbytes, cudaMemcpyHostToDevice, h->h2d_stream));
+  if (live) CUDA_TRY(cudaMemcpyAsync(sl.kv, packed_kv_host, live, cudaMemcpyHostToDevice, h->h2d_stream));
+  CUDA_TRY(cudaEventRecord(sl.loaded, h->h2d_stream));
+  CUDA_TRY(cudaStreamWaitEvent(st, sl.loaded, 0));
+  if (sl.used) CUDA_TRY(cudaStreamWaitEvent(st, sl.fetched, 0));
+  PCP_TRY(pcp_forward(h, sl.q, sl.kv, valid_len, sl.out, stream));
+  CUDA_TRY(cudaEventRecord(sl.done, st));
+  CUDA_TRY(cudaStreamWaitEvent(h->d2h_stream, sl.done, 0));
+  CUDA_TRY(cudaMemcpyAsync(out_host, sl.out, qbytes, cudaMemcpyDeviceToHost, h->d2h_stream));
+  CUDA_TRY(cudaEventRecord(sl.fetched, h->d2h_stream));
+  sl.used = true;
+  h->next_slot ^= 1;
+  return PCP_OK;
+}
+
+int pcp_forward_host_wait(pcp_handle_t* h) {
+  if (!h) return fail(PCP_ERR_INVALID_ARGUMENT, "handle is NULL");
+  CUDA_TRY(cudaSetDevice(h->device));
+  if (h->h2d_stream) {
+    CUDA_TRY(cudaStreamSynchronize(h->h2d_stream));
+    CUDA_TRY(cudaStreamSynchronize(h->d2h_stream));
+  }
+  return PCP_OK;
+}
+
+int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
+                     void* out_host, void* stream) {
+  PCP_TRY(pcp_forward_host_async(h, q_host, packed_kv_host, valid_len, out_host, stream));
+  PCP_TRY(pcp_forward_host_wait(h));
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
   return PCP_OK;
 }
 
@@ -1766,9 +1816,20 @@ int pcp_destroy(pcp_handle_t* h) {
   cudaFree(h->cur_k);
   cudaFree(h->cur_v);
   cudaFree(h->ws);
-  cudaFree(h->dq);
-  cudaFree(h->dkv);
-  cudaFree(h->dout);
+  if (h->h2d_stream) {
+    cudaStreamSynchronize(h->h2d_stream);
+    cudaStreamSynchronize(h->d2h_stream);
+  }
+  for (auto& sl : h->slots) {
+    cudaFree(sl.q);
+    cudaFree(sl.kv);
+    cudaFree(sl.out);
+    if (sl.loaded) cudaEventDestroy(sl.loaded);
+    if (sl.done) cudaEventDestroy(sl.done);
+    if (sl.fetched) cudaEventDestroy(sl.fetched);
+  }
+  if (h->h2d_stream) cudaStreamDestroy(h->h2d_stream);
+  if (h->d2h_stream) cudaStreamDestroy(h->d2h_stream);
   delete h;
   return PCP_OK;
 }

@@ -324,6 +324,36 @@ class HistoryAttention:
             )
         return out
 
+    def forward_host_async(self, q: torch.Tensor, packed_kv: torch.Tensor, valid_len=None,
+                           out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """``forward_host`` without waiting (``pcp_forward_host_async``): the
+        copies and the forward are enqueued and the call returns; one call's
+        copies overlap the previous call's forward.  ``q``, ``packed_kv`` and
+        ``out`` should be pinned; keep them unmodified (and do not read ``out``)
+        until ``forward_host_wait``."""
+        cfg = self.config
+        if q.device.type != "cpu" or packed_kv.device.type != "cpu":
+            raise ValueError("forward_host_async takes CPU tensors")
+        if tuple(q.shape) != (cfg.num_q_heads, cfg.local_q_len, cfg.head_dim) or q.dtype != torch.bfloat16:
+            raise ValueError("bad Q")
+        if tuple(packed_kv.shape) != (cfg.max_local_blocks, payload_elements(cfg)) or packed_kv.dtype != self.kv_dtype:
+            raise ValueError("bad packed KV")
+        if out is None:
+            out = torch.empty_like(q, pin_memory=True)
+        vals = self._valid(valid_len)
+        with torch.cuda.device(self.device):
+            _capi.check(
+                _capi.lib().pcp_forward_host_async(
+                    self._handle, ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(packed_kv.data_ptr()), vals,
+                    ctypes.c_void_p(out.data_ptr()), _cuda_stream_ptr(stream)
+                )
+            )
+        return out
+
+    def forward_host_wait(self) -> None:
+        """Waits for every ``forward_host_async`` of this handle."""
+        _capi.check(_capi.lib().pcp_forward_host_wait(self._handle))
+
     def status(self, timeout_ms: int = 60000) -> None:
         """Wait for the last call and raise on device timeouts / ring failures."""
         _capi.check(_capi.lib().pcp_device_status(self._handle, int(timeout_ms)))

@@ -278,9 +278,23 @@ int pcp_forward_prefill(pcp_handle_t* h, int32_t interleave_size, const void* q,
                         const int32_t* valid_len, const void* k_cur, const void* v_cur, void* out, void* stream);
 
 /* Same as pcp_forward, with HOST buffers (pinned or pageable): copies q and packed_kv in,
- * runs pcp_forward on `stream`, copies out back, and synchronises `stream`. */
+ * runs pcp_forward on `stream`, copies out back, and returns when out_host is
+ * filled (the end-to-end call of run_poc.py:241-257: host tensors in, .cpu() out). */
 int pcp_forward_host(pcp_handle_t* h, const void* q_host, const void* packed_kv_host, const int32_t* valid_len,
                      void* out_host, void* stream);
+
+/* The asynchronous form for a serving loop: enqueues the host->device copies
+ * (a copy stream of the handle), pcp_forward on `stream` and the copy of out
+ * back (a second copy stream), and returns at once.  The handle alternates
+ * two device staging slots, so one call's copies overlap the previous call's
+ * forward.  Host buffers should be pinned (pageable ones make the copies
+ * synchronous); they must stay valid and unmodified, and out_host must not
+ * be read, until pcp_forward_host_wait returns.  Not in the reference, whose
+ * driver loop is synchronous (run_poc.py:289-318). */
+int pcp_forward_host_async(pcp_handle_t* h, const void* q_host, const void* packed_kv_host,
+                           const int32_t* valid_len, void* out_host, void* stream);
+/* Waits for every pcp_forward_host_async of the handle (copies included). */
+int pcp_forward_host_wait(pcp_handle_t* h);
 
 /* Waits up to timeout_ms for the last forward (compute and ring streams) and
  * reports failures: device-side wait timeouts, CUDA errors, NCCL async errors

@@ -189,6 +189,37 @@ def ring_graph(rank, world, kv_path=None):
     return {"metrics": worst, "ring_bytes": stats["ring_bytes"], "attn_launches": stats["attn_launches"]}
 
 
+def ring_host_async(rank, world):
+    """The serving-loop host entry at two ranks: pinned host inputs, several
+    asynchronous steps, every output against the oracle."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from aws_training_study_b200.pcp_attention import PCPAttentionConfig
+    from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
+    from parity import assert_parity, expected_rank_output, make_case, packed_shards
+
+    P, cur, mh, ah, bs, I, hq, hkv, d, kv = CASES["qwen_d256_fp8"]
+    cfg = PCPAttentionConfig(P, cur, mh, ah, bs, I, hq, hkv, d).validate()
+    torch.cuda.set_device(rank)
+    q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=29)
+    packed = packed_shards(cfg, k_shards, v_shards)
+    attn = HistoryAttention(cfg, rank=rank, device=rank)
+    qh = q_shards[rank].pin_memory()
+    kvh = packed[rank].view(torch.uint8).pin_memory().view(packed[rank].dtype)
+    outs = [torch.empty_like(qh).pin_memory() for _ in range(4)]
+    for o in outs:
+        attn.forward_host_async(qh, kvh, out=o)
+    attn.forward_host_wait()
+    attn.status(120000)
+    want = expected_rank_output(cfg, q, k, v, rank)
+    m = [assert_parity(o, want, f"host async rank {rank} step {i}") for i, o in enumerate(outs)]
+    st = attn.stats()
+    attn.close()
+    return {"metrics": m, "ring_bytes": st["ring_bytes"], "attn_launches": st["attn_launches"]}
+
+
 def ring_paged_inplace(rank, world):
     return ring_paged(rank, world, kv_path="in_place")
 
@@ -201,7 +232,7 @@ def ring_graph_inplace(rank, world):
 @pytest.mark.parametrize("fn", ["ring_qwen", "ring_ragged", "ring_qwen_storeforward", "ring_ragged_allgather",
                                 "prefill_ragged", "ring_paged", "ring_graph", "ring_qwen_pipeline",
                                 "ring_qwen_inplace", "ring_qwen_storeforward_inplace", "ring_qwen_pipeline_inplace",
-                                "ring_paged_inplace", "ring_graph_inplace"])
+                                "ring_paged_inplace", "ring_graph_inplace", "ring_host_async"])
 def test_two_rank_ring_matches_oracle(fn):
     res = run_ranks("test_gpu_ring", fn, 2, timeout=600, backend="gloo", env={"NCCL_NVLS_ENABLE": "0"})
     assert len(res) == 2, res
