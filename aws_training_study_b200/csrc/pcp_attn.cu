@@ -22,6 +22,7 @@
 
 #include "attn_pair.cuh"
 #include "attn_pair_sk.cuh"
+#include "attn_pair2.cuh"
 #include "attn_kv.cuh"
 #include "kv_stage.cuh"
 
@@ -229,6 +230,18 @@ int64_t rows_per_head(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q
 int64_t total_rows(const pcp_dims_t& d) { return static_cast<int64_t>(d.num_q_heads) * d.local_q_len; }
 // Work units of one split: 256-row CTA-pair tiles over every KV head.
 int64_t m_units(const pcp_dims_t& d) { return d.num_kv_heads * ceil_div(rows_per_head(d), pcp::kPairRows); }
+// Dense static-schedule history launches at head dim 128 with at least 512
+// query rows per KV head run on attn_fwd_pair2_kernel (two query tiles per
+// CTA pair, ping-pong), whose work units are 512 query rows.
+bool pingpong(const pcp_dims_t& d, bool in_place) {
+  return d.head_dim == 128 && !in_place && rows_per_head(d) >= pcp::Pair2Roles::kUnitRows;
+}
+// Work units of a static-schedule history launch.
+int64_t static_units(const pcp_dims_t& d, bool in_place) {
+  return pingpong(d, in_place) ? d.num_kv_heads * ceil_div(rows_per_head(d), pcp::Pair2Roles::kUnitRows)
+                               : m_units(d);
+}
+
 // Relative cost of a plan in key tiles per SM pair: stream-K walks
 // ceil(steps / pairs) tiles plus ~2 tiles of prologue and partial write;
 // static runs waves of (tiles per item + 2).
@@ -247,10 +260,11 @@ double plan_cost(const SplitPlan& pl, int64_t units, int64_t n_kt, int sms) {
 SplitPlan plan_splits(const pcp_dims_t& d, int64_t tiles, int64_t keys, int sms, int slot_cap, bool last,
                       bool in_place) {
   const int64_t n_kt = std::max<int64_t>(1, tiles);
-  const SplitPlan st = plan_static(m_units(d), n_kt, sms, slot_cap);
+  const int64_t su = static_units(d, in_place);
+  const SplitPlan st = plan_static(su, n_kt, sms, slot_cap);
   if (!last || kv_bytes(d, keys, in_place) > kStreamKMaxKvBytes) return st;
   const SplitPlan sk = plan_stream_k(m_units(d), n_kt, sms, slot_cap);
-  return plan_cost(sk, m_units(d), n_kt, sms) <= plan_cost(st, m_units(d), n_kt, sms) ? sk : st;
+  return plan_cost(sk, m_units(d), n_kt, sms) <= plan_cost(st, su, n_kt, sms) ? sk : st;
 }
 
 // A plan made for `planned` tiles run over `actual` >= planned tiles (in
@@ -419,6 +433,22 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
   // Two CTAs (one cluster) per pair; the cluster shape is compiled in.
   // Stream-K: a fixed set of pairs; static: one pair per unit and split.
   const bool sk = plan.mode == kModeStreamK;
+  if (!sk && causal.stripe_width == 0 && pingpong(d, false)) {
+    // Two query tiles per pair: units of 512 rows.
+    const int64_t mt2 = ceil_div(R, pcp::Pair2Roles::kUnitRows);
+    p.m_tiles_per_head = static_cast<int>(mt2);
+    const dim3 grid2(static_cast<unsigned>(2 * d.num_kv_heads * mt2), static_cast<unsigned>(plan.splits));
+    static int done2 = 0;
+    PCP_TRY(set_smem_attr(pcp::attn_fwd_pair2_kernel<128>, pcp::Pair2Smem<128>::kAlloc, &done2));
+    pcp::attn_fwd_pair2_kernel<128><<<grid2, pcp::Pair2Roles::kThreads, pcp::Pair2Smem<128>::kAlloc, st>>>(
+        tq, tk, tv, to, p);
+    CUDA_TRY(cudaGetLastError());
+    if (lc) {
+      lc->kernels++;
+      lc->attn++;
+    }
+    return PCP_OK;
+  }
   dim3 grid = sk ? dim3(static_cast<unsigned>(2 * plan.pairs), 1)
                             : dim3(static_cast<unsigned>(2 * d.num_kv_heads * mt), static_cast<unsigned>(plan.splits));
   if (d.head_dim == 256) {
@@ -1028,7 +1058,7 @@ int forward_impl(pcp_handle* h, const void* q, const LocalKV& local, const int32
       probe.sms = 0;
       plan_part(d, &probe, h->sms, max_splits);
       const bool local_fills_gpu =
-          probe.keys && m_units(d) * probe.plan.splits >= std::max(1, h->sms / 2);
+          probe.keys && static_units(d, in_place) * probe.plan.splits >= std::max(1, h->sms / 2);
       const int groups = (P >= 4 && !reserve && local_fills_gpu) ? 2 : 1;
       const int split_step = 1 + (P - 1 + 1) / 2;
       for (int g = 0; g < groups; ++g) {
