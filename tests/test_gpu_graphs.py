@@ -95,3 +95,29 @@ def test_length_above_bucket_is_reported(case, kv_path):
     with pytest.raises(_capi.PcpError, match="code 110"):
         attn.status()
     attn.close()
+
+
+def test_device_lengths_at_head_dim_128(kv_path):
+    """Device-length mode through the head-dim-128 kernels (the two-query-tile
+    ping-pong kernel on the dense path, the in-place kernel otherwise):
+    lengths below the bound and a recorded graph replayed inside it."""
+    cfg = PCPAttentionConfig(1, 1024, 8192, 8192, 512, 64, 16, 4, 128)
+    q, k, v, q_shards, k_shards, v_shards = make_case(cfg, seed=37)
+    qd, packed = q_shards[0].to(DEV), packed_shards(cfg, k_shards, v_shards)[0].to(DEV)
+    oc = oracle_config(cfg)
+
+    def expected(hist):
+        return orc.dense_history_attention(to_numpy_f32(q), to_numpy_f32(k[:, :hist]), to_numpy_f32(v[:, :hist]),
+                                           oc.softmax_scale)
+
+    attn = HistoryAttention(cfg, rank=0, device=0)
+    for hist in (1, 2000, 8192):
+        out = attn.forward_bucketed(qd, packed, torch.tensor([hist], dtype=torch.int32, device=DEV), [8192])
+        attn.status()
+        assert_parity(out, expected(hist), f"d128 bucket 8192 len {hist}")
+    g = BucketGraph(attn, [4096], qd, packed)
+    for hist in (4096, 2500):
+        out = g.replay([hist]).clone()
+        attn.status()
+        assert_parity(out, expected(hist), f"d128 graph len {hist}")
+    attn.close()
