@@ -21,8 +21,14 @@
 // TMEM), B = K split by keys / V split by head dim between the two CTAs, one
 // thread of the leader issues every cta_group::2 MMA, TMA loads counted on
 // the leader's barriers (no multicast), speculative P with lazy rescale.
-// Warps 0-7 are tile A's two softmax warpgroups, 8-15 tile B's, warp 16 the
-// TMA producer, warp 17 the MMA issuer.  Non-causal history launches with a
+// Warps 0-7 are tile A's two softmax warpgroups, 8-15 tile B's; warps 16-19
+// form the control warpgroup: warp 16 the TMA producer, warp 17 the MMA
+// issuer, 18-19 idle.  The control warpgroup exists so that registers can
+// move: launched at 96 per thread (640 threads, one CTA per SM), it drops to
+// 64 and each softmax thread rises to 104, which its 64 S values, 16 packed
+// P words and the row state need: no role spills (at 96 for all, the softmax
+// spilled; 112 for the softmax leaves 32 for the TMA and MMA loops, which
+// then spill).  Non-causal history launches with a
 // dense bf16 K/V; one item per (512-row unit, key split).
 #pragma once
 
@@ -40,12 +46,24 @@ struct Pair2Roles {
   static constexpr int kWGPerTile = 2;
   static constexpr int kSoftmaxThreads = 128 * kWGPerTile * kTiles;  // 512
   static constexpr int kTileThreads = 128 * kWGPerTile;              // 256 per query tile
-  static constexpr int kThreads = kSoftmaxThreads + 64;              // 576
+  static constexpr int kThreads = kSoftmaxThreads + 128;             // 640
   static constexpr int kProducerWarp = kSoftmaxThreads / 32;         // 16
   static constexpr int kMmaWarp = kProducerWarp + 1;                 // 17
+  // Registers per thread: at launch (what 640 threads x 1 CTA leave of the
+  // SM's 65536, in steps of 8), then softmax / control warpgroups.
+  static constexpr int kLaunchRegs = 96;
+  static constexpr int kSoftmaxRegs = 104;
+  static constexpr int kCtlRegs = 64;
   static constexpr int kKeys = kTileN / kWGPerTile;                  // 64 keys per softmax thread
   static constexpr int kUnitRows = 2 * kPairRows;                    // 512 query rows per pair
 };
+static_assert(Pair2Roles::kSoftmaxThreads * Pair2Roles::kSoftmaxRegs + 128 * Pair2Roles::kCtlRegs <=
+                  Pair2Roles::kThreads * Pair2Roles::kLaunchRegs,
+              "register split exceeds the launch's pool");
+// Per SM sub-partition: four softmax warps and one control warp.
+static_assert((4 * Pair2Roles::kSoftmaxRegs + Pair2Roles::kCtlRegs) * 32 <= 16384 &&
+                  5 * 32 * Pair2Roles::kLaunchRegs <= 16384,
+              "register split exceeds a sub-partition's register file");
 
 template <int D>
 struct Pair2Smem {
@@ -141,129 +159,136 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Roles::kThreads
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == R::kProducerWarp) {
-    // ------------------------------------------------------ TMA producer --
-    if (lane == 0 && n > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      if (leader) mbar_arrive_expect_tx(bar_q, 2 * 2 * L::kQBytes);
-      const uint32_t q_lead = mapa_shared(bar_q, 0);
-      for (int t = 0; t < 2; ++t)
-        for (int b = 0; b < D / kBoxCols; ++b)
-          tma_load_3d_pair(sQ + t * L::kQBytes + b * kBoxBytes, &tm_q, b * kBoxCols, tile_row0(t), head, q_lead);
-      uint32_t c = 0;
-      bool ok = true;
-      // Item order = first-use order of the MMAs: K_0, then (V_j, K_{j+1}).
-      auto issue = [&](bool is_v, int kt) {
-        const int st = c % NS;
-        if (!mbar_wait(bar_kv_empty(st), ((c / NS) & 1u) ^ 1u, abort_flag, p.err, kErrWaitKvEmpty)) return false;
-        if (leader) mbar_arrive_expect_tx(bar_kv_full(st), 2 * L::kStageBytes);
-        const uint32_t full_lead = mapa_shared(bar_kv_full(st), 0);
-        const uint32_t dst = sStage + st * L::kStageBytes;
-        if (!is_v) {
+  // Register split (setmaxnreg, warpgroup-uniform).  Each warpgroup's
+  // setmaxnreg sits at the top of its own branch: ptxas gives every region
+  // one register budget, and a join between the setmaxnreg and a role's code
+  // would leave that code with the smaller one.
+  if (warp >= R::kProducerWarp) {
+    setmaxnreg_dec<R::kCtlRegs>();
+    if (warp == R::kProducerWarp) {
+      // ------------------------------------------------------ TMA producer --
+      if (lane == 0 && n > 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        if (leader) mbar_arrive_expect_tx(bar_q, 2 * 2 * L::kQBytes);
+        const uint32_t q_lead = mapa_shared(bar_q, 0);
+        for (int t = 0; t < 2; ++t)
           for (int b = 0; b < D / kBoxCols; ++b)
-            tma_load_3d_pair(dst + b * L::kKBox, &tm_k, b * kBoxCols, kt * kTileN + static_cast<int>(rank) * 64,
-                             head, full_lead);
-        } else {
-          for (int b = 0; b < D / 2 / kBoxCols; ++b)
-            tma_load_3d_pair(dst + b * L::kVBox, &tm_v, static_cast<int>(rank) * (D / 2) + b * kBoxCols,
-                             kt * kTileN, head, full_lead);
+            tma_load_3d_pair(sQ + t * L::kQBytes + b * kBoxBytes, &tm_q, b * kBoxCols, tile_row0(t), head, q_lead);
+        uint32_t c = 0;
+        bool ok = true;
+        // Item order = first-use order of the MMAs: K_0, then (V_j, K_{j+1}).
+        auto issue = [&](bool is_v, int kt) {
+          const int st = c % NS;
+          if (!mbar_wait(bar_kv_empty(st), ((c / NS) & 1u) ^ 1u, abort_flag, p.err, kErrWaitKvEmpty)) return false;
+          if (leader) mbar_arrive_expect_tx(bar_kv_full(st), 2 * L::kStageBytes);
+          const uint32_t full_lead = mapa_shared(bar_kv_full(st), 0);
+          const uint32_t dst = sStage + st * L::kStageBytes;
+          if (!is_v) {
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_load_3d_pair(dst + b * L::kKBox, &tm_k, b * kBoxCols, kt * kTileN + static_cast<int>(rank) * 64,
+                               head, full_lead);
+          } else {
+            for (int b = 0; b < D / 2 / kBoxCols; ++b)
+              tma_load_3d_pair(dst + b * L::kVBox, &tm_v, static_cast<int>(rank) * (D / 2) + b * kBoxCols,
+                               kt * kTileN, head, full_lead);
+          }
+          ++c;
+          return true;
+        };
+        ok = issue(false, kt0);
+        for (int j = 0; j < n && ok; ++j) {
+          ok = issue(true, kt0 + j);
+          if (ok && j + 1 < n) ok = issue(false, kt0 + j + 1);
         }
-        ++c;
-        return true;
-      };
-      ok = issue(false, kt0);
-      for (int j = 0; j < n && ok; ++j) {
-        ok = issue(true, kt0 + j);
-        if (ok && j + 1 < n) ok = issue(false, kt0 + j + 1);
-      }
-      if (!ok) {
-        // Abort: let copies already in flight land before the CTA exits.
-        if (leader) {
-          for (uint32_t i = (c > (uint32_t)NS ? c - NS : 0); i < c; ++i)
-            mbar_wait_teardown(bar_kv_full(i % NS), (i / NS) & 1u);
-          mbar_wait_teardown(bar_q, 0);
-        } else {
-          const uint64_t t0 = globaltimer_ns();
-          while (globaltimer_ns() - t0 < 2000000ull) {
+        if (!ok) {
+          // Abort: let copies already in flight land before the CTA exits.
+          if (leader) {
+            for (uint32_t i = (c > (uint32_t)NS ? c - NS : 0); i < c; ++i)
+              mbar_wait_teardown(bar_kv_full(i % NS), (i / NS) & 1u);
+            mbar_wait_teardown(bar_q, 0);
+          } else {
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 2000000ull) {
+            }
           }
         }
       }
-    }
-    __syncwarp();
-  } else if (warp == R::kMmaWarp) {
-    // --------------------------------------------- MMA issuer (leader only) --
-    if (leader && lane == 0 && n > 0) {
-      constexpr uint32_t idesc_qk = make_idesc_bf16(kPairRows, kTileN, false, false);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(kPairRows, D, false, true);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.err, kErrWaitQ);
-      tc_fence_after();
-      // Stage of item c (K_0 = 0, V_j = 2j + 1, K_{j+1} = 2j + 2); the first
-      // use of an item waits for its bytes.
-      auto wait_item = [&](uint32_t c) {
-        if (!mbar_wait(bar_kv_full(c % NS), (c / NS) & 1u, abort_flag, p.err, kErrWaitKvFull)) return false;
+      __syncwarp();
+    } else if (warp == R::kMmaWarp) {
+      // --------------------------------------------- MMA issuer (leader only) --
+      if (leader && lane == 0 && n > 0) {
+        constexpr uint32_t idesc_qk = make_idesc_bf16(kPairRows, kTileN, false, false);
+        constexpr uint32_t idesc_pv = make_idesc_bf16(kPairRows, D, false, true);
+        bool ok = mbar_wait(bar_q, 0, abort_flag, p.err, kErrWaitQ);
         tc_fence_after();
-        return true;
-      };
-      auto qk = [&](int t, uint32_t c) {
-        const uint32_t s_tmem = tmem + kTmemS0 + t * kTileN;
-        const uint32_t qbase = sQ + t * L::kQBytes;
-        const uint32_t kbase = sStage + (c % NS) * L::kStageBytes;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qa = qbase + (kk / 4) * kBoxBytes + (kk % 4) * 32;
-          const uint32_t kb = kbase + (kk / 4) * L::kKBox + (kk % 4) * 32;
-          umma_ss_pair(s_tmem, make_sw128_desc(qa, 16, 1024), make_sw128_desc(kb, 16, 1024), idesc_qk,
-                       kk != 0 ? 1u : 0u);
+        // Stage of item c (K_0 = 0, V_j = 2j + 1, K_{j+1} = 2j + 2); the first
+        // use of an item waits for its bytes.
+        auto wait_item = [&](uint32_t c) {
+          if (!mbar_wait(bar_kv_full(c % NS), (c / NS) & 1u, abort_flag, p.err, kErrWaitKvFull)) return false;
+          tc_fence_after();
+          return true;
+        };
+        auto qk = [&](int t, uint32_t c) {
+          const uint32_t s_tmem = tmem + kTmemS0 + t * kTileN;
+          const uint32_t qbase = sQ + t * L::kQBytes;
+          const uint32_t kbase = sStage + (c % NS) * L::kStageBytes;
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qa = qbase + (kk / 4) * kBoxBytes + (kk % 4) * 32;
+            const uint32_t kb = kbase + (kk / 4) * L::kKBox + (kk % 4) * 32;
+            umma_ss_pair(s_tmem, make_sw128_desc(qa, 16, 1024), make_sw128_desc(kb, 16, 1024), idesc_qk,
+                         kk != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(bar_s_full(t), kBothCtas);
+        };
+        auto pv = [&](int t, uint32_t c, int j) {
+          if (!mbar_wait(bar_p_full(t), j & 1, abort_flag, p.err, kErrWaitPFull)) return false;
+          tc_fence_after();
+          const uint32_t p_tmem = tmem + kTmemS0 + t * kTileN;
+          const uint32_t o_tmem = tmem + t * D;
+          const uint32_t vbase = sStage + (c % NS) * L::kStageBytes;
+  #pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk) {
+            // A = P (packed into the first half of each warpgroup's 64 S
+            // columns), B = V half, MN-major (see attn_pair.cuh).
+            const uint32_t a_cols = kk * 8 + (kk >= 4 ? 32 : 0);
+            umma_ts_pair(o_tmem, p_tmem + a_cols, make_sw128_desc(vbase + kk * 2048, L::kVBox, 1024), idesc_pv,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(bar_o(t), kBothCtas);
+          return true;
+        };
+        if (ok) ok = wait_item(0);
+        if (ok) {
+          qk(0, 0);
+          qk(1, 0);
+          umma_commit_pair(bar_kv_empty(0), kBothCtas);  // K_0 read by both tiles
         }
-        umma_commit_pair(bar_s_full(t), kBothCtas);
-      };
-      auto pv = [&](int t, uint32_t c, int j) {
-        if (!mbar_wait(bar_p_full(t), j & 1, abort_flag, p.err, kErrWaitPFull)) return false;
-        tc_fence_after();
-        const uint32_t p_tmem = tmem + kTmemS0 + t * kTileN;
-        const uint32_t o_tmem = tmem + t * D;
-        const uint32_t vbase = sStage + (c % NS) * L::kStageBytes;
-#pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk) {
-          // A = P (packed into the first half of each warpgroup's 64 S
-          // columns), B = V half, MN-major (see attn_pair.cuh).
-          const uint32_t a_cols = kk * 8 + (kk >= 4 ? 32 : 0);
-          umma_ts_pair(o_tmem, p_tmem + a_cols, make_sw128_desc(vbase + kk * 2048, L::kVBox, 1024), idesc_pv,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+        for (int j = 0; j < n && ok; ++j) {
+          const uint32_t cv = 2 * j + 1, ck = 2 * j + 2;
+          const bool more = j + 1 < n;
+          ok = wait_item(cv) && pv(0, cv, j);
+          if (ok && more) {
+            ok = wait_item(ck);
+            if (ok) qk(0, ck);
+          }
+          if (ok) ok = pv(1, cv, j);
+          if (ok) umma_commit_pair(bar_kv_empty(cv % NS), kBothCtas);  // V_j read by both tiles
+          if (ok && more) {
+            qk(1, ck);
+            umma_commit_pair(bar_kv_empty(ck % NS), kBothCtas);  // K_{j+1} read by both tiles
+          }
         }
-        umma_commit_pair(bar_o(t), kBothCtas);
-        return true;
-      };
-      if (ok) ok = wait_item(0);
-      if (ok) {
-        qk(0, 0);
-        qk(1, 0);
-        umma_commit_pair(bar_kv_empty(0), kBothCtas);  // K_0 read by both tiles
+        // Drain: completes when every MMA issued above has.
+        umma_commit_pair(bar_td, kLeaderCta);
+        mbar_wait_teardown(bar_td, 0);
       }
-      for (int j = 0; j < n && ok; ++j) {
-        const uint32_t cv = 2 * j + 1, ck = 2 * j + 2;
-        const bool more = j + 1 < n;
-        ok = wait_item(cv) && pv(0, cv, j);
-        if (ok && more) {
-          ok = wait_item(ck);
-          if (ok) qk(0, ck);
-        }
-        if (ok) ok = pv(1, cv, j);
-        if (ok) umma_commit_pair(bar_kv_empty(cv % NS), kBothCtas);  // V_j read by both tiles
-        if (ok && more) {
-          qk(1, ck);
-          umma_commit_pair(bar_kv_empty(ck % NS), kBothCtas);  // K_{j+1} read by both tiles
-        }
-      }
-      // Drain: completes when every MMA issued above has.
-      umma_commit_pair(bar_td, kLeaderCta);
-      mbar_wait_teardown(bar_td, 0);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
+    setmaxnreg_inc<R::kSoftmaxRegs>();
     // ---------------------------------------- softmax / correction / epilogue --
     constexpr int kHalfKeys = R::kKeys;  // 64
     constexpr int kOCols = D / R::kWGPerTile;

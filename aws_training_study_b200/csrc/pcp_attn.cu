@@ -440,6 +440,17 @@ int launch_attention(const pcp_dims_t& d, const void* q, const Workspace& w, uin
     const dim3 grid2(static_cast<unsigned>(2 * d.num_kv_heads * mt2), static_cast<unsigned>(plan.splits));
     static int done2 = 0;
     PCP_TRY(set_smem_attr(pcp::attn_fwd_pair2_kernel<128>, pcp::Pair2Smem<128>::kAlloc, &done2));
+    // The kernel's register split (setmaxnreg) assumes its launch count: a
+    // build that compiled it with another one is refused, never launched.
+    static std::atomic<int> regs = 0;
+    if (regs.load() == 0) {
+      cudaFuncAttributes fa{};
+      CUDA_TRY(cudaFuncGetAttributes(&fa, pcp::attn_fwd_pair2_kernel<128>));
+      regs.store(fa.numRegs);
+    }
+    if (regs.load() != pcp::Pair2Roles::kLaunchRegs)
+      return fail(PCP_ERR_UNSUPPORTED, "attn_fwd_pair2_kernel has %d registers per thread; its split needs %d",
+                  regs.load(), pcp::Pair2Roles::kLaunchRegs);
     pcp::attn_fwd_pair2_kernel<128><<<grid2, pcp::Pair2Roles::kThreads, pcp::Pair2Smem<128>::kAlloc, st>>>(
         tq, tk, tv, to, p);
     CUDA_TRY(cudaGetLastError());

@@ -411,6 +411,19 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t two) {
   return pack_f16x2(__uint_as_float(two << 16), __uint_as_float(two & 0xFFFF0000u));
 }
 
+// Per-warpgroup register reallocation (all four warps of a warpgroup execute
+// it).  .inc blocks until the CTA's pool (its launch registers) has room, so
+// the shares of all warpgroups must add up to at most threads x launch
+// registers; callers check both at compile time and before launch.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
