@@ -252,7 +252,6 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
 
     from aws_training_study_b200.pcp_attention import PCPAttentionConfig
     from aws_training_study_b200.pcp_attention.cuda_backend import HistoryAttention
-    from aws_training_study_b200.pcp_attention.host import near_device
     from aws_training_study_b200.pcp_attention.inputs import make_local_baseline_inputs
 
     torch.cuda.set_device(local_rank)
@@ -338,13 +337,10 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
     # ---- end to end through the public API with host buffers -------------
     e2e = None
     if not args.no_e2e:
-        # With several ranks per host, each rank's pinned buffers are placed
-        # in its GPU's NUMA node (allocated while on the GPU's local cores).
-        with near_device(local_rank, enable=args.numa == "on" or (args.numa == "auto" and world > 1)) as near:
-            q_h = q.cpu().pin_memory()
-            kv_h = packed.view(torch.uint8).cpu().pin_memory().view(packed.dtype)
-            out_h = torch.empty_like(q_h).pin_memory()
-            out_h2 = torch.empty_like(q_h).pin_memory()
+        q_h = q.cpu().pin_memory()
+        kv_h = packed.view(torch.uint8).cpu().pin_memory().view(packed.dtype)
+        out_h = torch.empty_like(q_h).pin_memory()
+        out_h2 = torch.empty_like(q_h).pin_memory()
         for _ in range(2):
             attn.forward_host(q_h, kv_h, valid, out_h)
         barrier()
@@ -380,7 +376,6 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int) -> int:
             "api": "HistoryAttention.forward_host_async / forward_host_wait -> pcp_forward_host_async (C ABI), "
                    "pinned host buffers, a stream of steps (host wall clock, max over ranks)",
             "host_issue_ms_per_step": issue_ms,
-            "host_buffers": f"NUMA-local to the GPU ({near} cores)" if near else "default placement",
             "sync_call_ms_per_step": sync_ms,
             "sync_call_value": flops_step / (sync_ms / 1e3) / 1e12,
         }
@@ -677,9 +672,6 @@ def main() -> int:
     ap.add_argument("--current-len", type=int, default=None, help="override the workload's global Q (profiling)")
     ap.add_argument("--history", type=int, default=None, help="override the workload's history length (profiling)")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--numa", choices=["auto", "on", "off"], default="auto",
-                    help="allocate the e2e leg's pinned host buffers on the GPU's local CPU cores "
-                         "(auto: with more than one rank)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the full-output check after the timed steps")
