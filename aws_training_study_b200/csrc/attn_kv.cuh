@@ -516,23 +516,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKvThreads, 1)
     // (ex2.approx on the MUFU), stored as f16 over this warpgroup's S
     // columns; returns the fp32 sum.
     auto make_p = [&](const float* sv, float m, uint32_t t_s) {
-      const float neg = -m * sl2;
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c2 = 0; c2 < kHalfKeys / 32; ++c2) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(sv[c2 * 32 + 2 * i], sl2, neg));
-          const float p1 = ex2_approx(fmaf(sv[c2 * 32 + 2 * i + 1], sl2, neg));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack_f16x2(p0, p1);
-        }
-        tmem_st16(t_s + wg * kHalfKeys + c2 * 16, pk);
-      }
-      tmem_wait_st();
-      return sum0 + sum1;
+      return store_probs<kHalfKeys, true>(sv, m, sl2, t_s + wg * kHalfKeys);
     };
     uint32_t J = 0;
     if (n_kt == 0 && pair < units && kp.sched == kSchedStreamK) {
@@ -563,24 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKvThreads, 1)
         tc_fence_after();
         const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
         float s[kHalfKeys];
-        tmem_ld32(t_s + wg * kHalfKeys, s);
-        tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
-        tmem_wait_ld();
-        const int valid = tile_valid - wg * kHalfKeys;
-        if (valid < kHalfKeys) {
-#pragma unroll
-          for (int i = 0; i < kHalfKeys; ++i)
-            if (i >= valid) s[i] = -INFINITY;
-        }
-        float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-        for (int i = 4; i < kHalfKeys; i += 4) {
-          mx0 = fmaxf(mx0, s[i]);
-          mx1 = fmaxf(mx1, s[i + 1]);
-          mx2 = fmaxf(mx2, s[i + 2]);
-          mx3 = fmaxf(mx3, s[i + 3]);
-        }
-        const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        load_scores<kHalfKeys>(t_s + wg * kHalfKeys, tile_valid - wg * kHalfKeys, s);
+        const float pmax = row_max(s);
         red[(b * kSoftmaxWarpgroups + wg) * kTileM + row] = pmax;
         mbar_arrive(bar_red(b));
         // Pass 0 (tiles after the first): speculative P with the current
@@ -615,17 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKvThreads, 1)
                           mbar_wait(bar_o((jg - 1) & 1), ((jg - 1) >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
           if (!ok) break;
           tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < kOCols / 32; ++c) {
-            float o[32];
-            const uint32_t t_o = t_row + wg * kOCols + c * 32;
-            tmem_ld32(t_o, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(t_o, o);
-          }
-          tmem_wait_st();
+          rescale_o<kOCols>(t_row + wg * kOCols, alpha);
         }
         tc_fence_before();
         __syncwarp();
@@ -659,37 +617,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kKvThreads, 1)
       named_bar_sync(2, kSoftmaxThreads);
       const float inv_l = 1.f / l_tot;
       if (final_out) {
-        __nv_bfloat16* dst = p.out + grow * D + wg * kOCols;
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          tmem_ld32(t_row + wg * kOCols + c * 32, o);
-          tmem_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
-          if (live) {
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              *reinterpret_cast<uint4*>(dst + c * 32 + q4 * 8) =
-                  make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-          }
-        }
+        store_o_bf16<kOCols>(t_row + wg * kOCols, inv_l, p.out + grow * D + wg * kOCols, live);
       } else {
         const size_t split_idx = static_cast<size_t>(p.split_base + sg.slot);
-        float* dst = p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols;
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          tmem_ld32(t_row + wg * kOCols + c * 32, o);
-          tmem_wait_ld();
-          if (live) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + c * 32 + i) =
-                  make_float4(o[i] * inv_l, o[i + 1] * inv_l, o[i + 2] * inv_l, o[i + 3] * inv_l);
-          }
-        }
+        store_o_partial<kOCols>(t_row + wg * kOCols, inv_l,
+                                p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols, live);
         if (live && wg == 0) {
           p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
           // The segment that ends a unit marks the unit's unused slots empty.

@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 
 #include "attn_common.cuh"
+#include "attn_softmax.cuh"
 #include "ptx.cuh"
 
 namespace pcp {
@@ -288,29 +289,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThrea
     // (ex2.approx on the MUFU; moving a share of them to an FMA-pipe
     // polynomial measured slower at both head dims).  Stores P (bf16) over
     // this warpgroup's S columns and returns the fp32 sum.
+    // P of keys [64 wg + 32 c2, +32) goes to TMEM columns [64 wg + 16 c2, +16):
+    // inside this warpgroup's own S columns, so the stores never touch S
+    // values the other warpgroup has yet to read.
     auto make_p = [&](const float* sv, float m, uint32_t t_s) {
-      const float neg = -m * sl2;
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c2 = 0; c2 < kHalfKeys / 32; ++c2) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float x0 = fmaf(sv[c2 * 32 + 2 * i], sl2, neg);
-          const float x1 = fmaf(sv[c2 * 32 + 2 * i + 1], sl2, neg);
-          const float p0 = ex2_approx(x0);
-          const float p1 = ex2_approx(x1);
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        // P of keys [64 wg + 32 c2, +32) as bf16 pairs -> TMEM columns
-        // [64 wg + 16 c2, +16): inside this warpgroup's own S columns, so the
-        // stores never touch S values the other warpgroup has yet to read.
-        tmem_st16(t_s + wg * kHalfKeys + c2 * 16, pk);
-      }
-      tmem_wait_st();
-      return sum0 + sum1;
+      return store_probs<kHalfKeys>(sv, m, sl2, t_s + wg * kHalfKeys);
     };
     for (int j = 0; j < n && ok; ++j) {
       const int b = j & 1;
@@ -319,24 +302,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThrea
       tc_fence_after();
       const uint32_t t_s = t_row + kTmemS0 + b * kTileN;
       float s[kHalfKeys];
-#pragma unroll
-      for (int c32 = 0; c32 < kHalfKeys / 32; ++c32) tmem_ld32(t_s + wg * kHalfKeys + 32 * c32, s + 32 * c32);
-      tmem_wait_ld();
-      const int valid = key_limit - (kt0 + j) * kTileN - wg * kHalfKeys;
-      if (valid < kHalfKeys) {
-#pragma unroll
-        for (int i = 0; i < kHalfKeys; ++i)
-          if (i >= valid) s[i] = -INFINITY;
-      }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int i = 4; i < kHalfKeys; i += 4) {
-        mx0 = fmaxf(mx0, s[i]);
-        mx1 = fmaxf(mx1, s[i + 1]);
-        mx2 = fmaxf(mx2, s[i + 2]);
-        mx3 = fmaxf(mx3, s[i + 3]);
-      }
-      const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      load_scores<kHalfKeys>(t_s + wg * kHalfKeys, key_limit - (kt0 + j) * kTileN - wg * kHalfKeys, s);
+      const float pmax = row_max(s);
       // Publish this half's max (double-buffered by tile parity; a
       // warpgroup is at most one tile ahead of the other).
       red[(b * kWG + wg) * kTileM + row] = pmax;
@@ -371,17 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThrea
                         mbar_wait(bar_o((j - 1) & 1), ((j - 1) >> 1) & 1u, abort_flag, p.err, kErrWaitODone));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          const uint32_t t_o = t_row + wg * kOCols + c * 32;
-          tmem_ld32(t_o, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(t_o, o);
-        }
-        tmem_wait_st();
+        rescale_o<kOCols>(t_row + wg * kOCols, alpha);
       }
       // One arrive per warp on the leader's P barrier (all lanes' TMEM stores
       // are complete: tcgen05.wait::st is warp-collective).
@@ -402,25 +359,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThrea
       for (int w = 1; w < kWG; ++w) l_tot += red[(wg ^ w) * kTileM + row];
       const float inv_l = 1.f / l_tot;
       if (p.write_final) {
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          const int col = wg * kOCols + c * 32;
-          tmem_ld32(t_row + col, o);
-          tmem_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
-          const int box = col / kBoxCols;
-          uint8_t* rowp = smem + L::kQOff + box * kBoxBytes + row * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = ((col % kBoxCols) / 8) + q;
-            const int phys = chunk ^ (row & 7);
-            *reinterpret_cast<uint4*>(rowp + phys * 16) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
-        }
+        // bf16 O through the Q buffer (every QK^T is complete) and a TMA store.
+        stage_o_sw128<kOCols>(t_row + wg * kOCols, inv_l, smem + L::kQOff, kBoxBytes, wg * kOCols, row);
         fence_proxy_async_smem();
         named_bar_sync(3, R::kSoftmaxThreads);
         if (threadIdx.x == 0 && row0 < p.rows_per_head) {  // no store of a tile wholly past the rows
@@ -435,18 +375,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairRoles<D>::kThrea
         const size_t grow = static_cast<size_t>(head) * p.rows_per_head + rih;
         float* dst = p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols;
         const bool live = rih < p.rows_per_head;
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          tmem_ld32(t_row + wg * kOCols + c * 32, o);
-          tmem_wait_ld();
-          if (live) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + c * 32 + i) =
-                  make_float4(o[i] * inv_l, o[i + 1] * inv_l, o[i + 2] * inv_l, o[i + 3] * inv_l);
-          }
-        }
+        store_o_partial<kOCols>(t_row + wg * kOCols, inv_l, dst, live);
         if (live && wg == 0) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
       }
     } else if (n <= 0 && !p.write_final && wg == 0) {

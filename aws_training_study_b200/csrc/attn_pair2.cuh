@@ -306,49 +306,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Roles::kThreads
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = n > 0;
-    auto make_p = [&](const float* sv, float m) {
-      const float neg = -m * sl2;
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c2 = 0; c2 < kHalfKeys / 32; ++c2) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(sv[c2 * 32 + 2 * i], sl2, neg));
-          const float p1 = ex2_approx(fmaf(sv[c2 * 32 + 2 * i + 1], sl2, neg));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(t_s + wg * kHalfKeys + c2 * 16, pk);
-      }
-      tmem_wait_st();
-      return sum0 + sum1;
-    };
+    auto make_p = [&](const float* sv, float m) { return store_probs<kHalfKeys>(sv, m, sl2, t_s + wg * kHalfKeys); };
     for (int j = 0; j < n && ok; ++j) {
       const int b = j & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(t), j & 1, abort_flag, p.err, kErrWaitSFull));
       if (!ok) break;
       tc_fence_after();
       float s[kHalfKeys];
-      tmem_ld32(t_s + wg * kHalfKeys, s);
-      tmem_ld32(t_s + wg * kHalfKeys + 32, s + 32);
-      tmem_wait_ld();
-      const int valid = key_limit - (kt0 + j) * kTileN - wg * kHalfKeys;
-      if (valid < kHalfKeys) {
-#pragma unroll
-        for (int i = 0; i < kHalfKeys; ++i)
-          if (i >= valid) s[i] = -INFINITY;
-      }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int i = 4; i < kHalfKeys; i += 4) {
-        mx0 = fmaxf(mx0, s[i]);
-        mx1 = fmaxf(mx1, s[i + 1]);
-        mx2 = fmaxf(mx2, s[i + 2]);
-        mx3 = fmaxf(mx3, s[i + 3]);
-      }
-      const float pmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      load_scores<kHalfKeys>(t_s + wg * kHalfKeys, key_limit - (kt0 + j) * kTileN - wg * kHalfKeys, s);
+      const float pmax = row_max(s);
       red_t[(b * 2 + wg) * kTileM + row] = pmax;
       mbar_arrive(bar_red(t, b));
       // Speculative P with the current reference max (see attn_pair.cuh).
@@ -369,19 +335,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Roles::kThreads
       l += tile_sum;
       // S_t(j) ready means PV_t(j-1) is complete (issued before QK_t(j), and
       // the tensor pipe completes in order): O_t may be rescaled right away.
-      if (j > 0 && redo) {
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          const uint32_t a = t_o + wg * kOCols + c * 32;
-          tmem_ld32(a, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(a, o);
-        }
-        tmem_wait_st();
-      }
+      if (j > 0 && redo) rescale_o<kOCols>(t_o + wg * kOCols, alpha);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(mapa_shared(bar_p_full(t), 0));
@@ -398,25 +352,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Roles::kThreads
       if (p.write_final) {
         // This tile's Q buffer holds its bf16 O for the TMA store (every
         // QK^T of both tiles completed before the last PV of either).
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          const int col = wg * kOCols + c * 32;
-          tmem_ld32(t_o + col, o);
-          tmem_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
-          const int box = col / kBoxCols;
-          uint8_t* rowp = smem + L::kQOff + t * L::kQBytes + box * kBoxBytes + row * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = ((col % kBoxCols) / 8) + q;
-            const int phys = chunk ^ (row & 7);
-            *reinterpret_cast<uint4*>(rowp + phys * 16) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
-        }
+        stage_o_sw128<kOCols>(t_o + wg * kOCols, inv_l, smem + L::kQOff + t * L::kQBytes, kBoxBytes, wg * kOCols,
+                              row);
         fence_proxy_async_smem();
         named_bar_sync(bar_base + 2, R::kTileThreads);
         if ((threadIdx.x & (R::kTileThreads - 1)) == 0 && row0 < p.rows_per_head) {
@@ -431,18 +368,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Roles::kThreads
         const size_t grow = static_cast<size_t>(head) * p.rows_per_head + rih;
         float* dst = p.part_o + (split_idx * p.total_rows + grow) * D + wg * kOCols;
         const bool live = rih < p.rows_per_head;
-#pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
-          float o[32];
-          tmem_ld32(t_o + wg * kOCols + c * 32, o);
-          tmem_wait_ld();
-          if (live) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + c * 32 + i) =
-                  make_float4(o[i] * inv_l, o[i + 1] * inv_l, o[i + 2] * inv_l, o[i + 3] * inv_l);
-          }
-        }
+        store_o_partial<kOCols>(t_o + wg * kOCols, inv_l, dst, live);
         if (live && wg == 0) p.part_lse[split_idx * p.total_rows + grow] = m_ref * sl2 + __log2f(l_tot);
       }
     } else if (n <= 0 && !p.write_final && wg == 0) {
