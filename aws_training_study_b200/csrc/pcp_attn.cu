@@ -810,15 +810,23 @@ namespace {
 int wait_nccl(ncclComm_t comm, ncclResult_t r, int timeout_ms) {
   if (r == ncclSuccess) return PCP_OK;
   if (r != ncclInProgress) return fail(PCP_ERR_NCCL, "NCCL: %s", ncclGetErrorString(r));
+  // A non-blocking communicator finishes enqueueing a group on its own
+  // thread, usually within microseconds: poll with yields for the first
+  // 2 ms (a forward's host path must stay well under its device time), then
+  // with short sleeps up to the timeout.
   const auto t0 = std::chrono::steady_clock::now();
   ncclResult_t st = ncclInProgress;
   while (true) {
     ncclCommGetAsyncError(comm, &st);
     if (st != ncclInProgress) break;
-    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+    const auto waited = std::chrono::steady_clock::now() - t0;
+    if (waited > std::chrono::milliseconds(timeout_ms)) {
       return fail(PCP_ERR_PEER, "NCCL operation still in progress after %d ms (peer missing?)", timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (waited < std::chrono::milliseconds(2))
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
   if (st != ncclSuccess) return fail(PCP_ERR_NCCL, "NCCL async error: %s", ncclGetErrorString(st));
   return PCP_OK;
