@@ -135,7 +135,7 @@ def main() -> int:
     import pcp_attention.config as refcfg
 
     importlib.reload(refcfg)
-    from pcp_attention.config import PCPAttentionConfig as Cfg, get_preset as gp
+    from pcp_attention.config import get_preset as gp
 
     lay = {}
     for total, P, I in ((2048, 4, 64), (1024, 4, 16), (8192, 8, 64), (131072, 8, 64)):
