@@ -602,7 +602,7 @@ void add_source(const pcp_dims_t& d, Part* part, const uint8_t* base, const int3
 
 // Key tiles a part's launch walks: per source when in place, over the
 // compacted keys otherwise.
-int64_t part_tiles(const pcp_dims_t& d, const Part& part) {
+int64_t part_tiles(const Part& part) {
   return part.in_place ? part.tiles : ceil_div(part.keys, pcp::kTileN);
 }
 
@@ -611,10 +611,10 @@ int plan_part(const pcp_dims_t& d, Part* part, int sms, int max_splits) {
   if (part->sms > 0 && part->sms < sms) {
     // A launch that shares the GPU with an exchange: a persistent grid on
     // part->sms SMs (stream-K; the caller checked that its K/V fits in L2).
-    part->plan = plan_stream_k(m_units(d), part_tiles(d, *part), part->sms, max_splits);
+    part->plan = plan_stream_k(m_units(d), part_tiles(*part), part->sms, max_splits);
     return PCP_OK;
   }
-  part->plan = plan_splits(d, part_tiles(d, *part), part->keys, sms, max_splits, part->last, part->in_place);
+  part->plan = plan_splits(d, part_tiles(*part), part->keys, sms, max_splits, part->last, part->in_place);
   return PCP_OK;
 }
 
@@ -705,7 +705,7 @@ int64_t dense_keys(int64_t keys, bool in_place) { return in_place ? 0 : keys; }
 SplitPlan stateless_plan(const pcp_dims_t& d, const Part& part, int slot_cap) {
   const SplitPlan pl =
       plan_splits(d, ceil_div(part.keys, pcp::kTileN), part.keys, num_sms(), slot_cap, true, part.in_place);
-  return fit_plan(pl, part_tiles(d, part));
+  return fit_plan(pl, part_tiles(part));
 }
 
 // The launches of one stateless history part: its attention (in place, or
@@ -1499,7 +1499,7 @@ int pcp_history_attention_noalloc(const pcp_dims_t* dims, const void* q, const v
     if (part.keys == 0) return fail(PCP_ERR_INVALID_ARGUMENT, "no valid history tokens");
     int split_cap = max_splits_for(d);
     while (true) {
-      part.plan = plan_splits(d, part_tiles(d, part), part.keys, sms, split_cap, true, part.in_place);
+      part.plan = plan_splits(d, part_tiles(part), part.keys, sms, split_cap, true, part.in_place);
       w = ws_layout(d, dense_keys(part.keys, part.in_place), part.plan.splits);
       if (w.total <= PCP_NOALLOC_SCRATCH_BYTES) return PCP_OK;
       if (part.plan.splits == 1)
