@@ -106,3 +106,19 @@ def test_workspace_size_is_host_only():
     bad = _capi.PcpDims(1, 4096, 256, 512, 32, 2, 96, 0)
     assert lib.pcp_history_attention_workspace_size(ctypes.byref(bad), 10, ctypes.byref(n)) == 2  # UNSUPPORTED
     assert b"head_dim" in lib.pcp_last_error()
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No silent fallback: with the extension absent, loading it raises."""
+    import subprocess
+    import sys
+
+    code = (
+        "import pathlib, aws_training_study_b200._capi as c\n"
+        f"c.LIB_PATH = pathlib.Path({str(tmp_path / 'absent.so')!r})\n"
+        "try:\n    c.lib()\nexcept ImportError as e:\n    print('raised:', e)\n"
+    )
+    r = subprocess.run([sys.executable, "-c", code], cwd=Path(__file__).resolve().parents[1], capture_output=True,
+                       text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert "raised:" in r.stdout and "no fallback" in r.stdout
